@@ -1,0 +1,200 @@
+// grxDNN host library for B200: handle, validation, dispatch.
+//
+// The reference has no grxDNN code (planned only: docs/designs/
+// grxcp_architecture.md:594, docs/designs/grxcp_roadmap.md:860-876), so the
+// validation rules here are this library's own, written in grxBLAS's style
+// (reference src/libs/grxblas/grxblas.cpp:498-524): null handle ->
+// NOT_INITIALIZED, malformed arguments -> INVALID_VALUE, empty problem ->
+// SUCCESS without a launch, a type or shape the kernels do not implement ->
+// NOT_SUPPORTED (never a slower substitute).
+#include <cuda_runtime.h>
+
+#include <mutex>
+
+#include "attention.cuh"
+#include "grx/grxdnn.h"
+#include "host_common.h"
+#include "kernels.h"
+
+struct grxdnnContext {
+  cudaStream_t stream = nullptr;
+  std::mutex mutex;
+  grx::DeviceState dev;
+};
+
+namespace {
+
+grxdnnStatus_t from_cuda(cudaError_t e) {
+  switch (e) {
+    case cudaSuccess: return GRXDNN_STATUS_SUCCESS;
+    case cudaErrorMemoryAllocation: return GRXDNN_STATUS_ALLOC_FAILED;
+    case cudaErrorInvalidValue: return GRXDNN_STATUS_INVALID_VALUE;
+    case cudaErrorNotSupported: return GRXDNN_STATUS_NOT_SUPPORTED;
+    case cudaErrorNoKernelImageForDevice:
+    case cudaErrorInvalidDeviceFunction: return GRXDNN_STATUS_ARCH_MISMATCH;
+    default: return GRXDNN_STATUS_EXECUTION_FAILED;
+  }
+}
+
+grxdnnStatus_t ensure(grxdnnContext& ctx, bool need_tensor) {
+  std::lock_guard<std::mutex> lock(ctx.mutex);
+  const int rc = grx::ensure_device(ctx.dev);
+  if (rc == 1) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (rc == 2) return GRXDNN_STATUS_ALLOC_FAILED;
+  if (need_tensor && ctx.dev.cc_major != 10) return GRXDNN_STATUS_ARCH_MISMATCH;
+  return GRXDNN_STATUS_SUCCESS;
+}
+
+int norm_dtype(grxDataType_t t) {
+  switch (t) {
+    case GRX_R_32F: return 0;
+    case GRX_R_16BF: return 1;
+    case GRX_R_16F: return 2;
+    default: return -1;
+  }
+}
+
+grxdnnStatus_t check_norm(grxdnnHandle_t h, int rows, int hidden, const void* x, grxDataType_t xt, long long ldx,
+                          const float* gamma, float eps, const void* y, grxDataType_t yt, long long ldy,
+                          bool& empty) {
+  empty = false;
+  if (!h) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (rows < 0 || hidden < 0) return GRXDNN_STATUS_INVALID_VALUE;
+  if (rows == 0) {
+    empty = true;
+    return GRXDNN_STATUS_SUCCESS;
+  }
+  if (hidden == 0) return GRXDNN_STATUS_INVALID_VALUE;
+  if (!x || !y || !gamma) return GRXDNN_STATUS_INVALID_VALUE;
+  if (ldx < hidden || ldy < hidden) return GRXDNN_STATUS_INVALID_VALUE;
+  if (!(eps >= 0.0f)) return GRXDNN_STATUS_INVALID_VALUE;
+  if (xt != yt || norm_dtype(xt) < 0) return GRXDNN_STATUS_NOT_SUPPORTED;
+  return GRXDNN_STATUS_SUCCESS;
+}
+
+bool same_shape(const grxdnnAttnTensor_t& a, const grxdnnAttnTensor_t& b) {
+  return a.batch == b.batch && a.heads == b.heads && a.seq == b.seq && a.headDim == b.headDim;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* grxdnnGetStatusString(grxdnnStatus_t s) {
+  switch (s) {
+    case GRXDNN_STATUS_SUCCESS: return "success";
+    case GRXDNN_STATUS_NOT_INITIALIZED: return "library not initialized (no usable device)";
+    case GRXDNN_STATUS_ALLOC_FAILED: return "allocation failed";
+    case GRXDNN_STATUS_INVALID_VALUE: return "invalid argument";
+    case GRXDNN_STATUS_ARCH_MISMATCH: return "device lacks a required capability (sm_100 tensor cores)";
+    case GRXDNN_STATUS_EXECUTION_FAILED: return "kernel execution failed";
+    case GRXDNN_STATUS_NOT_SUPPORTED: return "not supported";
+    case GRXDNN_STATUS_INTERNAL_ERROR: return "internal error";
+  }
+  return "unknown status";
+}
+
+grxdnnStatus_t grxdnnCreate(grxdnnHandle_t* handle) {
+  if (!handle) return GRXDNN_STATUS_INVALID_VALUE;
+  *handle = reinterpret_cast<grxdnnHandle_t>(new grxdnnContext());
+  return GRXDNN_STATUS_SUCCESS;
+}
+
+grxdnnStatus_t grxdnnDestroy(grxdnnHandle_t handle) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  auto* ctx = reinterpret_cast<grxdnnContext*>(handle);
+  grx::release_device(ctx->dev);
+  delete ctx;
+  return GRXDNN_STATUS_SUCCESS;
+}
+
+grxdnnStatus_t grxdnnSetStream(grxdnnHandle_t handle, grxStream_t stream) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  auto* ctx = reinterpret_cast<grxdnnContext*>(handle);
+  std::lock_guard<std::mutex> lock(ctx->mutex);
+  ctx->stream = reinterpret_cast<cudaStream_t>(stream);
+  return GRXDNN_STATUS_SUCCESS;
+}
+
+grxdnnStatus_t grxdnnGetStream(grxdnnHandle_t handle, grxStream_t* stream) {
+  if (!handle || !stream) return GRXDNN_STATUS_INVALID_VALUE;
+  *stream = reinterpret_cast<grxStream_t>(reinterpret_cast<grxdnnContext*>(handle)->stream);
+  return GRXDNN_STATUS_SUCCESS;
+}
+
+grxdnnStatus_t grxdnnRMSNormForward(grxdnnHandle_t handle, int rows, int hidden, const void* x,
+                                    grxDataType_t xType, long long ldx, const float* gamma, float eps, void* y,
+                                    grxDataType_t yType, long long ldy, float* rstd) {
+  bool empty;
+  grxdnnStatus_t s = check_norm(handle, rows, hidden, x, xType, ldx, gamma, eps, y, yType, ldy, empty);
+  if (s != GRXDNN_STATUS_SUCCESS || empty) return s;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  s = ensure(ctx, false);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  return from_cuda(
+      grx::launch_rmsnorm(rows, hidden, norm_dtype(xType), x, ldx, gamma, eps, y, ldy, rstd, ctx.stream));
+}
+
+grxdnnStatus_t grxdnnLayerNormForward(grxdnnHandle_t handle, int rows, int hidden, const void* x,
+                                      grxDataType_t xType, long long ldx, const float* gamma, const float* beta,
+                                      float eps, void* y, grxDataType_t yType, long long ldy, float* mean,
+                                      float* rstd) {
+  bool empty;
+  grxdnnStatus_t s = check_norm(handle, rows, hidden, x, xType, ldx, gamma, eps, y, yType, ldy, empty);
+  if (s != GRXDNN_STATUS_SUCCESS || empty) return s;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  s = ensure(ctx, false);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  return from_cuda(grx::launch_layernorm(rows, hidden, norm_dtype(xType), x, ldx, gamma, beta, eps, y, ldy, mean,
+                                         rstd, ctx.stream));
+}
+
+grxdnnStatus_t grxdnnAttentionForward(grxdnnHandle_t handle, const grxdnnAttnTensor_t* qd, const void* q,
+                                      const grxdnnAttnTensor_t* kd, const void* k, const grxdnnAttnTensor_t* vd,
+                                      const void* v, const grxdnnAttnTensor_t* od, void* o, float scale, int causal,
+                                      float* lse) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (!qd || !kd || !vd || !od) return GRXDNN_STATUS_INVALID_VALUE;
+  const grxdnnAttnTensor_t* all[4] = {qd, kd, vd, od};
+  for (auto* d : all)
+    if (d->batch < 0 || d->heads < 0 || d->seq < 0 || d->headDim <= 0 || d->strideSeq < d->headDim)
+      return GRXDNN_STATUS_INVALID_VALUE;
+  if (!same_shape(*qd, *od) || !same_shape(*kd, *vd)) return GRXDNN_STATUS_INVALID_VALUE;
+  if (qd->batch != kd->batch || qd->headDim != kd->headDim) return GRXDNN_STATUS_INVALID_VALUE;
+  if (qd->batch == 0 || qd->heads == 0 || qd->seq == 0) return GRXDNN_STATUS_SUCCESS;
+  if (!q || !k || !v || !o) return GRXDNN_STATUS_INVALID_VALUE;
+  if (!(scale > 0.0f) && !(scale < 0.0f)) return GRXDNN_STATUS_INVALID_VALUE;
+  if (causal && qd->seq != kd->seq) return GRXDNN_STATUS_NOT_SUPPORTED;
+  if (kd->seq == 0) return GRXDNN_STATUS_NOT_SUPPORTED;
+  for (auto* d : all)
+    if (d->dtype != GRX_R_16BF) return GRXDNN_STATUS_NOT_SUPPORTED;
+  if (qd->headDim != 128 || qd->heads != kd->heads) return GRXDNN_STATUS_NOT_SUPPORTED;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  grxdnnStatus_t s = ensure(ctx, true);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  grx::AttnArgs a{};
+  a.batch = qd->batch;
+  a.heads = qd->heads;
+  a.seq_q = qd->seq;
+  a.seq_k = kd->seq;
+  a.q = q; a.q_sb = qd->strideBatch; a.q_sh = qd->strideHead; a.q_ss = qd->strideSeq;
+  a.k = k; a.k_sb = kd->strideBatch; a.k_sh = kd->strideHead; a.k_ss = kd->strideSeq;
+  a.v = v; a.v_sb = vd->strideBatch; a.v_sh = vd->strideHead; a.v_ss = vd->strideSeq;
+  a.o = o; a.o_sb = od->strideBatch; a.o_sh = od->strideHead; a.o_ss = od->strideSeq;
+  a.lse = lse;
+  a.scale = scale;
+  a.causal = causal ? 1 : 0;
+  a.err_word = ctx.dev.err_word;
+  a.timeout_ns = grx::wait_timeout_ns();
+  return from_cuda(grx::launch_attention_fwd(a, ctx.dev.num_sms, ctx.stream));
+}
+
+grxdnnStatus_t grxdnnGetExecutionStatus(grxdnnHandle_t handle) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  auto* ctx = reinterpret_cast<grxdnnContext*>(handle);
+  std::lock_guard<std::mutex> lock(ctx->mutex);
+  const int code = grx::take_error(ctx->dev, ctx->stream);
+  return code == 0 ? GRXDNN_STATUS_SUCCESS : GRXDNN_STATUS_EXECUTION_FAILED;
+}
+
+}  // extern "C"

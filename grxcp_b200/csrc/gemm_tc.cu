@@ -1,0 +1,397 @@
+// Tensor-core GEMM for sm_100a: tcgen05.mma with TMEM accumulators, fed by TMA
+// through a multi-stage shared-memory ring, warp-specialised, persistent.
+//
+// Replaces the reference's hgemm_tcu / igemm_tcu kernels
+// (src/libs/grxblas/kernels/hgemm_tcu.cpp:215-382), which walk 8x4x8 WMMA
+// tiles from a single CTA. Semantics kept from there: column-major operands
+// with all four transposes, C = alpha*acc + beta*C with beta == 0 never reading
+// C (:354-357), the int8 epilogue in exact int32 arithmetic (:352-357), and
+// masked edge tiles that never touch ld padding (:339-361).
+//
+// CTA organisation (192 threads, one CTA per SM, grid = min(tiles, SMs)):
+//   warp 0      TMA producer: one thread streams A and B k-blocks into a
+//               kStages-deep ring of 128-byte-swizzled smem stages.
+//   warp 1      MMA issuer: one thread issues 4 tcgen05.mma per stage into a
+//               128 x 256 fp32/int32 accumulator in TMEM and commits the stage
+//               back to the producer; two accumulators (512 TMEM columns) let
+//               the epilogue of tile i overlap the main loop of tile i+1.
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (thread = output
+//               row, so a warp's stores down a column of C are contiguous),
+//               apply alpha / scales / beta*C / bias, convert, store.
+// Every mbarrier wait is bounded (ptx.cuh); a timeout aborts the CTA cleanly.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <mutex>
+
+#include "gemm_tc.cuh"
+#include "ptx.cuh"
+
+namespace grx {
+
+__device__ __forceinline__ void decode_tile(const TcGemmParams& p, int t, int& bt, int& mt, int& nt) {
+  const int tpb = p.m_tiles * p.n_tiles;
+  bt = t / tpb;
+  const int r = t - bt * tpb;
+  const int group = p.group_m * p.n_tiles;
+  const int g = r / group;
+  const int first = g * p.group_m;
+  const int gm = min(p.m_tiles - first, p.group_m);
+  const int w = r - g * group;
+  mt = first + w % gm;
+  nt = w / gm;
+}
+
+// Waits without honouring the abort flag: used only to let in-flight copies
+// and MMAs land before the CTA releases its shared memory and TMEM.
+static __device__ __noinline__ void wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns, int* err) {
+  const uint32_t addr = smem_u32(bar);
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(addr, parity)) {
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      if (err) atomicCAS(err, 0, kErrTimeoutDrain);
+      return;
+    }
+  }
+}
+
+template <int OUT>
+__device__ __forceinline__ float load_c(const void* c, long long idx) {
+  if constexpr (OUT == kOutF32) return static_cast<const float*>(c)[idx];
+  else if constexpr (OUT == kOutBF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(c)[idx]);
+  else return __half2float(static_cast<const __half*>(c)[idx]);
+}
+
+template <int OUT>
+__device__ __forceinline__ void store_c(void* c, long long idx, float v) {
+  if constexpr (OUT == kOutF32) static_cast<float*>(c)[idx] = v;
+  else if constexpr (OUT == kOutBF16) static_cast<__nv_bfloat16*>(c)[idx] = __float2bfloat16_rn(v);
+  else static_cast<__half*>(c)[idx] = __float2half_rn(v);
+}
+
+template <int KIND, int OUT>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ TcGemmParams p) {
+  constexpr int ES = (KIND == kKindF16) ? 2 : 1;  // element bytes
+  constexpr int BK = 128 / ES;                    // k per stage (one 128-byte swizzle row)
+  constexpr int UK = 32 / ES;                     // k per tcgen05.mma
+  constexpr int KSUB = BK / UK;                   // MMAs per stage
+  constexpr int ATOM = 128 / ES;                  // elements in one MN-major swizzle row
+  constexpr uint32_t kStageTx = kStageBytesA + kStageBytesB;
+
+  if (p.abi_version != kTcGemmAbi) {
+    if (threadIdx.x == 0 && p.err_word) atomicCAS(p.err_word, 0, kErrBadAbi);
+    return;
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages * kStageBytesA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kStages * kStageBytesB);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * kTileN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  WaitCtx wc{p.err_word, abort_flag, p.timeout_ns};
+  const int total = p.m_tiles * p.n_tiles * p.batch;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_par = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int bt, mt, nt;
+        decode_tile(p, t, bt, mt, nt);
+        const int ba = bt * p.a_batch_step, bb = bt * p.b_batch_step;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded(&empty[stage], phase ^ 1u, wc, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          uint64_t* fb = &full[stage];
+          mbar_arrive_expect_tx(fb, kStageTx);
+          issued_mask |= 1u << stage;
+          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+          uint8_t* a_dst = sA + stage * kStageBytesA;
+          uint8_t* b_dst = sB + stage * kStageBytesB;
+          const int k0 = kb * BK;
+          if (!p.a_mn_major) {
+            tma_load_3d(a_dst, &tmA, fb, k0, mt * kTileM, ba);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kTileM / ATOM; ++j)
+              tma_load_3d(a_dst + j * (BK * 128), &tmA, fb, mt * kTileM + j * ATOM, k0, ba);
+          }
+          if (!p.b_mn_major) {
+            tma_load_3d(b_dst, &tmB, fb, k0, nt * kTileN, bb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < kTileN / ATOM; ++j)
+              tma_load_3d(b_dst + j * (BK * 128), &tmB, fb, nt * kTileN + j * ATOM, k0, bb);
+          }
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every armed stage land before the CTA's shared memory goes away.
+        for (int s = 0; s < kStages; ++s)
+          if (issued_mask & (1u << s)) wait_drain(&full[s], (issued_par >> s) & 1u, p.timeout_ns, p.err_word);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
+        const int b = local & 1;
+        if (!wait_bounded(&tempty[b], ((local >> 1) & 1) ^ 1u, wc, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * kTileN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded(&full[stage], phase, wc, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * kStageBytesA);
+          const uint32_t b_addr = smem_u32(sB + stage * kStageBytesB);
+#pragma unroll
+          for (int kk = 0; kk < KSUB; ++kk) {
+            const uint64_t ad = p.a_mn_major ? sw128_desc(a_addr + kk * UK * 128, BK * 128, 1024)
+                                             : sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = p.b_mn_major ? sw128_desc(b_addr + kk * UK * 128, BK * 128, 1024)
+                                             : sw128_desc(b_addr + kk * 32, 16, 1024);
+            mma_ss<KIND>(d_tmem, ad, bd, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(&tfull[b]);
+      }
+      // Every MMA this thread issued must complete before TMEM is released.
+      mma_commit(drain);
+      wait_drain(drain, 0, p.timeout_ns, p.err_word);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
+      const int b = local & 1;
+      if (!wait_bounded(&tfull[b], (local >> 1) & 1, wc, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      int bt, mt, nt;
+      decode_tile(p, t, bt, mt, nt);
+      const int i = mt * kTileM + row;
+      const bool row_ok = i < p.m;
+      const long long cbase = (long long)bt * p.stride_c + i;
+      float rowmul = p.alpha;
+      if (p.scale_mode == 1) rowmul *= p.scale_a[bt * p.stride_sa] * p.scale_b[bt * p.stride_sb];
+      if (p.scale_mode == 2 && row_ok) rowmul *= p.scale_a[bt * p.stride_sa + i];
+      const float* sb = p.scale_b + bt * p.stride_sb;
+      const float* bias_f = static_cast<const float*>(p.bias) + bt * p.stride_bias;
+      const __nv_bfloat16* bias_h = static_cast<const __nv_bfloat16*>(p.bias) + bt * p.stride_bias;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + b * kTileN;
+      for (int c0 = 0; c0 < kTileN; c0 += 32) {
+        const int jbase = nt * kTileN + c0;
+        if (jbase >= p.n) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c0, r);
+        tmem_ld_wait();
+        if (row_ok) {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) {
+            const int j = jbase + jj;
+            if (j < p.n) {
+              const long long idx = cbase + (long long)j * p.ldc;
+              if constexpr (OUT == kOutS32) {
+                int v = p.ialpha * (int)r[jj];
+                if (p.beta_nonzero) v += p.ibeta * static_cast<const int*>(p.c)[idx];
+                static_cast<int*>(p.c)[idx] = v;
+              } else {
+                const float acc = (KIND == kKindI8) ? (float)(int)r[jj] : __uint_as_float(r[jj]);
+                float v = __fmul_rn(rowmul, acc);
+                if (p.scale_mode == 2) v = __fmul_rn(v, sb[j]);
+                if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
+                if (p.bias) v = __fadd_rn(v, p.bias_bf16 ? __bfloat162float(bias_h[j]) : bias_f[j]);
+                store_c<OUT>(p.c, idx, v);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * kTileN);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+bool tma_operand_ok(const void* base, long long ld, long long stride, int elem_bytes, int batch) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+  if ((ld * elem_bytes) % 16 != 0) return false;
+  if (batch > 1 && stride != 0) {
+    if (stride < 0) return false;
+    if ((stride * elem_bytes) % 16 != 0) return false;
+  }
+  return true;
+}
+
+// Operand tensor map: K-major -> dims {K, MN, batch}, box {BK, tile};
+// MN-major -> dims {MN, K, batch}, box {128 bytes of MN, BK}. 128-byte swizzle.
+static bool make_operand_map(CUtensorMap* map, const void* base, int es, int mn_major, long long mn_extent,
+                             long long k_extent, long long ld, long long stride, int batch_dim, int tile_mn) {
+  const int bk = 128 / es;
+  cuuint64_t dims[3], strides[2];
+  cuuint32_t box[3], estr[3] = {1, 1, 1};
+  if (!mn_major) {
+    dims[0] = (cuuint64_t)k_extent;
+    dims[1] = (cuuint64_t)mn_extent;
+    box[0] = bk;
+    box[1] = tile_mn;
+  } else {
+    dims[0] = (cuuint64_t)mn_extent;
+    dims[1] = (cuuint64_t)k_extent;
+    box[0] = 128 / es;
+    box[1] = bk;
+  }
+  dims[2] = (cuuint64_t)batch_dim;
+  box[2] = 1;
+  strides[0] = (cuuint64_t)(ld * es);
+  strides[1] = batch_dim > 1 ? (cuuint64_t)(stride * es) : (cuuint64_t)(ld * es) * dims[1];
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  const CUtensorMapDataType dt = es == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUresult r = enc(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int KIND, int OUT>
+static cudaError_t launch_impl(const CUtensorMap& ma, const CUtensorMap& mb, const TcGemmParams& p, int grid,
+                               cudaStream_t s) {
+  auto kfn = tc_gemm_kernel<KIND, OUT>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  kfn<<<grid, kGemmThreads, kGemmSmem, s>>>(ma, mb, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stream) {
+  const int es = L.kind == kKindF16 ? 2 : 1;
+  TcGemmParams p = L.p;
+  p.abi_version = kTcGemmAbi;
+  const int bk = 128 / es;
+  p.m_tiles = (p.m + kTileM - 1) / kTileM;
+  p.n_tiles = (p.n + kTileN - 1) / kTileN;
+  p.k_blocks = (p.k + bk - 1) / bk;
+  if (p.group_m <= 0) p.group_m = 16;
+  p.a_mn_major = L.a_mn_major;
+  p.b_mn_major = L.b_mn_major;
+  const uint32_t cfmt = (L.out == kOutS32) ? 2u : 1u;
+  p.idesc = make_idesc(cfmt, (uint32_t)L.a_fmt, (uint32_t)L.a_fmt, (uint32_t)L.a_mn_major, (uint32_t)L.b_mn_major,
+                       kTileM, kTileN);
+  const int a_bdim = (p.batch > 1 && L.stride_a != 0) ? p.batch : 1;
+  const int b_bdim = (p.batch > 1 && L.stride_b != 0) ? p.batch : 1;
+  p.a_batch_step = a_bdim > 1 ? 1 : 0;
+  p.b_batch_step = b_bdim > 1 ? 1 : 0;
+  CUtensorMap ma, mb;
+  if (!make_operand_map(&ma, L.a, es, L.a_mn_major, p.m, p.k, L.lda, L.stride_a, a_bdim, kTileM))
+    return cudaErrorInvalidValue;
+  if (!make_operand_map(&mb, L.b, es, L.b_mn_major, p.n, p.k, L.ldb, L.stride_b, b_bdim, kTileN))
+    return cudaErrorInvalidValue;
+  const long long tiles = (long long)p.m_tiles * p.n_tiles * p.batch;
+  if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
+  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  switch (L.kind * 4 + L.out) {
+    case kKindF16 * 4 + kOutF32: return launch_impl<kKindF16, kOutF32>(ma, mb, p, grid, stream);
+    case kKindF16 * 4 + kOutBF16: return launch_impl<kKindF16, kOutBF16>(ma, mb, p, grid, stream);
+    case kKindF16 * 4 + kOutF16: return launch_impl<kKindF16, kOutF16>(ma, mb, p, grid, stream);
+    case kKindI8 * 4 + kOutS32: return launch_impl<kKindI8, kOutS32>(ma, mb, p, grid, stream);
+    case kKindI8 * 4 + kOutBF16: return launch_impl<kKindI8, kOutBF16>(ma, mb, p, grid, stream);
+    case kKindI8 * 4 + kOutF32: return launch_impl<kKindI8, kOutF32>(ma, mb, p, grid, stream);
+    case kKindF8 * 4 + kOutBF16: return launch_impl<kKindF8, kOutBF16>(ma, mb, p, grid, stream);
+    case kKindF8 * 4 + kOutF32: return launch_impl<kKindF8, kOutF32>(ma, mb, p, grid, stream);
+    default: return cudaErrorNotSupported;
+  }
+}
+
+}  // namespace grx

@@ -1,0 +1,69 @@
+// Host/device interface of the tensor-core GEMM family (tcgen05 + TMA).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace grx {
+
+// Versioned argument block, passed by value as a __grid_constant__ parameter.
+// The kernel refuses to run on a version mismatch (the reference's kernel ABI
+// blocks do the same, src/libs/grxblas/hgemm_abi.h:20 and
+// src/libs/grxblas/kernels/sgemm.cpp:23-27).
+constexpr uint32_t kTcGemmAbi = 2;
+
+enum TcKind : int { kKindF16 = 0, kKindI8 = 1, kKindF8 = 2 };
+enum TcOut : int { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2, kOutS32 = 3 };
+
+struct TcGemmParams {
+  uint32_t abi_version;
+  int m, n, k, batch;
+  int a_mn_major, b_mn_major;      // smem layout of each operand
+  int a_batch_step, b_batch_step;  // 1: batch coordinate walks the tensor map, 0: broadcast
+  int m_tiles, n_tiles, k_blocks;
+  int group_m;                     // rasterisation band height in m-tiles
+  uint32_t idesc;                  // tcgen05 instruction descriptor
+  float alpha, beta;
+  int ialpha, ibeta;               // int32 epilogue (exact int8 path)
+  int beta_nonzero;
+  void* c;
+  long long ldc, stride_c;
+  const void* bias;
+  int bias_bf16;
+  long long stride_bias;
+  int scale_mode;                  // 0 none, 1 per-tensor, 2 per-row/per-column
+  const float* scale_a;
+  const float* scale_b;
+  long long stride_sa, stride_sb;
+  int* err_word;
+  unsigned long long timeout_ns;
+};
+
+struct TcGemmLaunch {
+  int kind;       // TcKind
+  int out;        // TcOut
+  int a_fmt;      // tcgen05 operand format code (f16 kind: 0 fp16, 1 bf16; i8: 1 signed; f8: 0 e4m3)
+  // Operand storage: element (r, kk) of op(X) at base + b*stride + (mn_major ? r + kk*ld : kk + r*ld)
+  const void* a; long long lda, stride_a; int a_mn_major;
+  const void* b; long long ldb, stride_b; int b_mn_major;
+  TcGemmParams p;
+};
+
+// Tile geometry shared by host and device.
+constexpr int kTileM = 128;
+constexpr int kTileN = 256;
+constexpr int kStages = 4;
+constexpr int kStageBytesA = kTileM * 128;   // 128 bytes of k per row
+constexpr int kStageBytesB = kTileN * 128;
+constexpr int kGemmThreads = 192;             // 6 warps: TMA, MMA, 4 x epilogue
+constexpr int kGemmSmem = kStages * (kStageBytesA + kStageBytesB) + 1024 /*align*/ + 256 /*barriers*/;
+
+// Enqueues the kernel (builds the TMA tensor maps). Returns cudaErrorInvalidValue
+// when an operand does not meet TMA alignment (the caller packs it first).
+cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stream);
+
+// True when an operand can be fed to TMA as stored.
+bool tma_operand_ok(const void* base, long long ld, long long stride, int elem_bytes, int batch);
+
+}  // namespace grx

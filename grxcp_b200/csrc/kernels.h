@@ -1,0 +1,53 @@
+// Host-callable launchers of the non-tcgen05 kernels. Each enqueues on the
+// given stream and returns the launch status; none synchronises.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "grx/grx_cycles.h"
+
+namespace grx {
+
+struct SgemmArgs {
+  int m, n, k, batch;
+  int ta, tb;
+  float alpha, beta;
+  const float* a; long long lda, stride_a;
+  const float* b; long long ldb, stride_b;
+  float* c; long long ldc, stride_c;
+  grxCycleSlot* probe;  // one slot per CTA, or null
+};
+cudaError_t launch_sgemm(const SgemmArgs& a, cudaStream_t s);
+// CTAs the sgemm kernel launches for an m x n problem (one probe slot each).
+int sgemm_ctas(int m, int n);
+
+// Copies op(X) (R rows of the MN extent by K) into a dense K-major buffer
+// dst[b][r][kk] with row pitch ldp elements. es = element bytes (1 or 2).
+cudaError_t launch_pack_kmajor(const void* src, int es, int src_mn_major, long long ld, long long stride, int batch,
+                               int rows, int k, void* dst, long long ldp, cudaStream_t s);
+
+// The k == 0 GEMM: C = beta*C (+ bias[j]) over the m x n window of every batch
+// member; out: 0 f32, 1 bf16, 2 f16, 3 s32 (integer beta).
+cudaError_t launch_gemm_k0(int out, void* c, long long ldc, long long stride_c, int m, int n, int batch,
+                           float beta, int ibeta, const void* bias, int bias_bf16, long long stride_bias,
+                           cudaStream_t s);
+
+cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y, int incy, cudaStream_t s);
+cudaError_t launch_sscal(int n, float alpha, float* x, int incx, cudaStream_t s);
+cudaError_t launch_sgemv(int trans, int m, int n, float alpha, const float* a, int lda, const float* x, int incx,
+                         float beta, float* y, int incy, cudaStream_t s);
+
+// Norms (norm.cu). dtype: 0 f32, 1 bf16, 2 f16 (x and y alike).
+cudaError_t launch_rmsnorm(int rows, int hidden, int dtype, const void* x, long long ldx, const float* gamma,
+                           float eps, void* y, long long ldy, float* rstd, cudaStream_t s);
+cudaError_t launch_layernorm(int rows, int hidden, int dtype, const void* x, long long ldx, const float* gamma,
+                             const float* beta, float eps, void* y, long long ldy, float* mean, float* rstd,
+                             cudaStream_t s);
+
+// Test hook: one CTA waits on an mbarrier nothing ever arrives at, through the
+// same bounded wait every kernel uses, and must come back with kErrTimeoutTest
+// in *err_word after about timeout_ns.
+cudaError_t launch_bounded_wait_probe(int* err_word, unsigned long long timeout_ns, cudaStream_t s);
+
+}  // namespace grx

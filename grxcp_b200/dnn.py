@@ -1,0 +1,95 @@
+"""grxDNN from Python: RMSNorm, LayerNorm and fused attention forward.
+
+Thin mirror of include/grx/grxdnn.h; every method returns the raw status code
+of the C call. Tensors are torch CUDA tensors (or integer device addresses).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+from . import _native as N
+from ._native import lib
+from .blas import dtype_code, ptr, stream_ptr
+
+
+class GrxdnnError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        super().__init__(f"{what}: {N.STATUS.get(status, status)} ({lib.grxdnnGetStatusString(status).decode()})")
+
+
+def check(status: int, what: str = "grxdnn") -> None:
+    if status != N.SUCCESS:
+        raise GrxdnnError(status, what)
+
+
+def attn_desc(t, batch=None, heads=None, seq=None, head_dim=None, dtype=None) -> N.grxdnnAttnTensor_t:
+    """Descriptor of a [batch, heads, seq, head_dim] tensor (strides in elements)."""
+    d = N.grxdnnAttnTensor_t()
+    if t is not None and hasattr(t, "stride"):
+        b, h, s, hd = t.shape
+        sb, sh, ss, sd = t.stride()
+        if sd != 1:
+            raise ValueError("head_dim must be contiguous")
+        d.batch, d.heads, d.seq, d.headDim = b, h, s, hd
+        d.strideBatch, d.strideHead, d.strideSeq = sb, sh, ss
+        d.dtype = dtype_code(t)
+    else:
+        d.batch, d.heads, d.seq, d.headDim = batch, heads, seq, head_dim
+        d.strideBatch, d.strideHead, d.strideSeq = heads * seq * head_dim, seq * head_dim, head_dim
+        d.dtype = dtype if dtype is not None else N.GRX_R_16BF
+    return d
+
+
+class Handle:
+    def __init__(self):
+        h = C.c_void_p()
+        check(lib.grxdnnCreate(C.byref(h)), "grxdnnCreate")
+        self.h = h
+
+    def close(self) -> int:
+        if self.h:
+            s = lib.grxdnnDestroy(self.h)
+            self.h = None
+            return s
+        return N.SUCCESS
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_stream(self, stream) -> int:
+        return lib.grxdnnSetStream(self.h, stream_ptr(stream))
+
+    def execution_status(self) -> int:
+        return lib.grxdnnGetExecutionStatus(self.h)
+
+    def rmsnorm(self, x, gamma, eps, y, rstd=None, rows=None, hidden=None, ldx=None, ldy=None) -> int:
+        rows = x.shape[0] if rows is None else rows
+        hidden = x.shape[1] if hidden is None else hidden
+        ldx = x.stride(0) if ldx is None else ldx
+        ldy = y.stride(0) if ldy is None else ldy
+        return lib.grxdnnRMSNormForward(self.h, rows, hidden, ptr(x), dtype_code(x), ldx, ptr(gamma), eps, ptr(y),
+                                        dtype_code(y), ldy, ptr(rstd))
+
+    def layernorm(self, x, gamma, beta, eps, y, mean=None, rstd=None, rows=None, hidden=None, ldx=None,
+                  ldy=None) -> int:
+        rows = x.shape[0] if rows is None else rows
+        hidden = x.shape[1] if hidden is None else hidden
+        ldx = x.stride(0) if ldx is None else ldx
+        ldy = y.stride(0) if ldy is None else ldy
+        return lib.grxdnnLayerNormForward(self.h, rows, hidden, ptr(x), dtype_code(x), ldx, ptr(gamma), ptr(beta),
+                                          eps, ptr(y), dtype_code(y), ldy, ptr(mean), ptr(rstd))
+
+    def attention(self, q, k, v, o, scale, causal, lse=None, descs=None) -> int:
+        dq, dk, dv, do = descs if descs is not None else (attn_desc(q), attn_desc(k), attn_desc(v), attn_desc(o))
+        return lib.grxdnnAttentionForward(self.h, C.byref(dq), ptr(q), C.byref(dk), ptr(k), C.byref(dv), ptr(v),
+                                          C.byref(do), ptr(o), scale, 1 if causal else 0, ptr(lse))

@@ -1,0 +1,92 @@
+/* grxcp-b200 -- grxDNN: transformer primitives on B200 (sm_100a).
+ *
+ * The reference plans a grxDNN library beside grxBLAS (docs/designs/
+ * grxcp_architecture.md:594, docs/designs/grxcp_roadmap.md:860-876,
+ * src/libs/CMakeLists.txt:12) but ships no header, code or tests for it. This
+ * header is therefore new; it follows grxBLAS's conventions so a caller of one
+ * knows the other: an opaque handle bound to a stream, status codes with the
+ * same values as grxblasStatus_t, device pointers for tensors, host values for
+ * scalars, no host synchronisation inside a call, and refusal (never a silent
+ * fallback) for anything the kernels do not implement.
+ */
+#ifndef GRXDNN_H
+#define GRXDNN_H
+
+#include "grx_runtime.h"
+#include "grx_types.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct grxdnnContext* grxdnnHandle_t;
+
+typedef enum {
+  GRXDNN_STATUS_SUCCESS          = 0,
+  GRXDNN_STATUS_NOT_INITIALIZED  = 1,
+  GRXDNN_STATUS_ALLOC_FAILED     = 2,
+  GRXDNN_STATUS_INVALID_VALUE    = 3,
+  GRXDNN_STATUS_ARCH_MISMATCH    = 4,
+  GRXDNN_STATUS_EXECUTION_FAILED = 5,
+  GRXDNN_STATUS_NOT_SUPPORTED    = 6,
+  GRXDNN_STATUS_INTERNAL_ERROR   = 7
+} grxdnnStatus_t;
+
+const char*    grxdnnGetStatusString(grxdnnStatus_t s);
+grxdnnStatus_t grxdnnCreate(grxdnnHandle_t* handle);
+grxdnnStatus_t grxdnnDestroy(grxdnnHandle_t handle);
+grxdnnStatus_t grxdnnSetStream(grxdnnHandle_t handle, grxStream_t stream);
+grxdnnStatus_t grxdnnGetStream(grxdnnHandle_t handle, grxStream_t* stream);
+
+/* RMSNorm forward over the last dimension of a [rows, hidden] matrix:
+ *   y[r, c] = x[r, c] * rsqrt(mean_c(x[r, :]^2) + eps) * gamma[c]
+ * Statistics in fp32. x/y: GRX_R_16BF (or GRX_R_16F, GRX_R_32F, same type for
+ * both); ldx/ldy are row pitches in elements (>= hidden). gamma is fp32
+ * [hidden]. rstd (fp32 [rows]) may be NULL. rows == 0 is SUCCESS. */
+grxdnnStatus_t grxdnnRMSNormForward(grxdnnHandle_t handle, int rows, int hidden,
+                                    const void* x, grxDataType_t xType, long long ldx,
+                                    const float* gamma, float eps,
+                                    void* y, grxDataType_t yType, long long ldy,
+                                    float* rstd);
+
+/* LayerNorm forward over the last dimension:
+ *   y[r, c] = (x[r, c] - mu_r) * rsqrt(var_r + eps) * gamma[c] + beta[c]
+ * with population variance, statistics in fp32. beta may be NULL (no shift);
+ * mean and rstd (fp32 [rows]) may be NULL. Types and pitches as RMSNorm. */
+grxdnnStatus_t grxdnnLayerNormForward(grxdnnHandle_t handle, int rows, int hidden,
+                                      const void* x, grxDataType_t xType, long long ldx,
+                                      const float* gamma, const float* beta, float eps,
+                                      void* y, grxDataType_t yType, long long ldy,
+                                      float* mean, float* rstd);
+
+/* A [batch, heads, seq, headDim] tensor with element strides; the headDim
+ * stride is 1. */
+typedef struct {
+  int           batch, heads, seq, headDim;
+  long long     strideBatch, strideHead, strideSeq;
+  grxDataType_t dtype;
+} grxdnnAttnTensor_t;
+
+/* Fused scaled-dot-product attention forward:
+ *   O = softmax(scale * Q K^T + mask) V,   lse = log(sum exp(scale * Q K^T + mask))
+ * per (batch, head). causal != 0 masks key j > query i (requires equal q/k
+ * sequence lengths). dtype GRX_R_16BF (Q, K, V, O alike), headDim 128, equal
+ * head counts. lse is fp32 [batch, heads, seqQ] contiguous (natural log), may
+ * be NULL. The softmax runs in fp32, both contractions accumulate in fp32 on
+ * the tensor cores. */
+grxdnnStatus_t grxdnnAttentionForward(grxdnnHandle_t handle,
+                                      const grxdnnAttnTensor_t* qDesc, const void* q,
+                                      const grxdnnAttnTensor_t* kDesc, const void* k,
+                                      const grxdnnAttnTensor_t* vDesc, const void* v,
+                                      const grxdnnAttnTensor_t* oDesc, void* o,
+                                      float scale, int causal, float* lse);
+
+/* Synchronises the handle's stream; EXECUTION_FAILED if a kernel launched
+ * through this handle gave up on a bounded wait since the last query. */
+grxdnnStatus_t grxdnnGetExecutionStatus(grxdnnHandle_t handle);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GRXDNN_H */

@@ -1,0 +1,211 @@
+"""CPU oracle for grxcp-b200 -- TEST INFRASTRUCTURE, never the product path.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs import
+this package, and only as the checker (or as the timed CPU baseline). It wraps
+``liboracle.so`` (oracle.c, plain gcc) with numpy; see oracle.c for the
+reference file:line each function restates.
+
+Parity status: the GEMM gates (fp32 sgemm, fp16 exact GemmEx, int8 -> int32)
+are pinned by the reference's own test-gate loops and known-answer tests, and
+the fp32 sgemm kernel is additionally pinned against the reference's sgemm
+kernel source compiled for the host (oracle/_ref, built by build_ref.py). bf16
+/ fp8 / scaled-int8 GEMM, RMSNorm, LayerNorm and attention have no code in the
+reference: for those the oracle is the fp64 definition, parity unpinned by the
+reference itself.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "liboracle.so"
+
+
+def build(force: bool = False) -> Path:
+    src = HERE / "oracle.c"
+    if force or not LIB_PATH.exists() or LIB_PATH.stat().st_mtime < src.stat().st_mtime:
+        cmd = ["gcc", "-O2", "-std=c11", "-fPIC", "-shared", "-ffp-contract=off", "-fno-fast-math", "-o",
+               str(LIB_PATH), str(src), "-lm", "-lpthread"]
+        subprocess.run(cmd, check=True)
+    return LIB_PATH
+
+
+build()
+_lib = C.CDLL(str(LIB_PATH))
+
+_vp = C.c_void_p
+_i = C.c_int
+_ll = C.c_longlong
+_f = C.c_float
+_d = C.c_double
+
+_protos = {
+    "ora_f32_to_bf16": (C.c_uint16, [_f]),
+    "ora_bf16_to_f32": (_f, [C.c_uint16]),
+    "ora_f32_to_f16": (C.c_uint16, [_f]),
+    "ora_f16_to_f32": (_f, [C.c_uint16]),
+    "ora_f32_to_e4m3": (C.c_uint8, [_f]),
+    "ora_e4m3_to_f32": (_f, [C.c_uint8]),
+    "ora_encode": (None, [_i, _vp, _vp, _ll]),
+    "ora_decode": (None, [_i, _vp, _vp, _ll]),
+    "ora_sgemm_ref": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
+    "ora_sgemm_kernel": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _ll, _vp, _i, _ll, _f, _vp, _i, _ll, _i]),
+    "ora_gemm_f32seq": (None, [_i, _i, _i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
+    "ora_igemm": (None, [_i, _i, _i, _i, _i, _i, _vp, _i, _vp, _i, _i, _vp, _i]),
+    "ora_igemm_npu": (None, [_i, _i, _i, _i, _i, _vp, _i, _vp, _i, _vp, _i]),
+    "ora_gemm_f64": (
+        None,
+        [_i, _i, _i, _i, _i, _d, _vp, _i, _ll, _vp, _i, _ll, _d, _vp, _vp, _i, _ll, _i, _vp, _ll, _i, _vp, _vp, _ll,
+         _ll, _i, _i, _i],
+    ),
+    "ora_rmsnorm": (None, [_i, _i, _vp, _ll, _vp, _d, _vp, _vp, _i]),
+    "ora_layernorm": (None, [_i, _i, _vp, _ll, _vp, _vp, _d, _vp, _vp, _vp, _i]),
+    "ora_attention": (None, [_i, _i, _i, _i, _vp, _vp, _vp, _d, _i, _vp, _i, _i, _i, _vp, _vp, _i]),
+}
+for _n, (_r, _a) in _protos.items():
+    getattr(_lib, _n).restype = _r
+    getattr(_lib, _n).argtypes = _a
+
+KIND = {"bf16": 0, "f16": 1, "e4m3": 2}
+
+
+def _p(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(_vp)
+
+
+def nthreads_default() -> int:
+    return max(1, len(os.sched_getaffinity(0)))
+
+
+# ------------------------------------------------------------ conversions
+
+def encode(kind: str, x) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint8 if kind == "e4m3" else np.uint16)
+    _lib.ora_encode(KIND[kind], _p(x), _p(out), x.size)
+    return out
+
+
+def decode(kind: str, bits) -> np.ndarray:
+    bits = np.ascontiguousarray(bits)
+    out = np.empty(bits.shape, dtype=np.float32)
+    _lib.ora_decode(KIND[kind], _p(bits), _p(out), bits.size)
+    return out
+
+
+def round_to(kind: str, x) -> np.ndarray:
+    """Values of x after rounding to `kind` (RNE; e4m3 saturating)."""
+    return decode(kind, encode(kind, x))
+
+
+# ------------------------------------------------------------ GEMM
+
+def sgemm_ref(ta, tb, m, n, k, alpha, A, lda, B, ldb, beta, Cbuf, ldc) -> np.ndarray:
+    """tests/libs/test_grxblas.cpp:63-80 on column-major float buffers; returns a new C buffer."""
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    out = np.array(Cbuf, dtype=np.float32, copy=True)
+    _lib.ora_sgemm_ref(int(ta), int(tb), m, n, k, alpha, _p(A), lda, _p(B), ldb, beta, _p(out), ldc)
+    return out
+
+
+def sgemm_kernel(ta, tb, m, n, k, alpha, A, lda, sA, B, ldb, sB, beta, Cbuf, ldc, sC, batch) -> np.ndarray:
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    out = np.array(Cbuf, dtype=np.float32, copy=True)
+    _lib.ora_sgemm_kernel(int(ta), int(tb), m, n, k, alpha, _p(A), lda, sA, _p(B), ldb, sB, beta, _p(out), ldc, sC,
+                          batch)
+    return out
+
+
+def gemm_f32seq(ta, tb, m, n, k, alpha, A, lda, B, ldb, beta, Cbuf, ldc) -> np.ndarray:
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    out = np.array(Cbuf, dtype=np.float32, copy=True)
+    _lib.ora_gemm_f32seq(int(ta), int(tb), m, n, k, alpha, _p(A), lda, _p(B), ldb, beta, _p(out), ldc)
+    return out
+
+
+def igemm(ta, tb, m, n, k, alpha, A, lda, B, ldb, beta, Cbuf, ldc) -> np.ndarray:
+    A = np.ascontiguousarray(A, np.int8)
+    B = np.ascontiguousarray(B, np.int8)
+    out = np.array(Cbuf, dtype=np.int32, copy=True)
+    _lib.ora_igemm(int(ta), int(tb), m, n, k, int(alpha), _p(A), lda, _p(B), ldb, int(beta), _p(out), ldc)
+    return out
+
+
+def igemm_npu(m, n, k, alpha, beta, A, lda, B, ldb, Cbuf, ldc) -> np.ndarray:
+    A = np.ascontiguousarray(A, np.int8)
+    B = np.ascontiguousarray(B, np.int8)
+    out = np.array(Cbuf, dtype=np.int32, copy=True)
+    _lib.ora_igemm_npu(m, n, k, alpha, beta, _p(A), lda, _p(B), ldb, _p(out), ldc)
+    return out
+
+
+def gemm_f64(ta, tb, m, n, k, alpha, A, lda, B, ldb, beta=0.0, Cin=None, ldc=None, sA=0, sB=0, sC=0, batch=1,
+             bias=None, sBias=0, scale_mode=0, sa=None, sb=None, ssa=0, ssb=0, j0=0, j1=None, nthreads=None,
+             out=None) -> np.ndarray:
+    """fp64 D = alpha*s*op(A)op(B) + beta*Cin + bias over columns [j0, j1); A/B are float arrays
+    holding the exact decoded input values. Returns the column-major fp64 buffer."""
+    ldc = m if ldc is None else ldc
+    j1 = n if j1 is None else j1
+    A = np.ascontiguousarray(A, np.float32)
+    B = np.ascontiguousarray(B, np.float32)
+    size = (batch - 1) * sC + ldc * n if batch > 1 else ldc * n
+    if out is None:
+        out = np.zeros(size, dtype=np.float64)
+    cin = None if Cin is None else np.ascontiguousarray(Cin, np.float64)
+    bias = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    sa = None if sa is None else np.ascontiguousarray(sa, np.float32)
+    sb = None if sb is None else np.ascontiguousarray(sb, np.float32)
+    _lib.ora_gemm_f64(int(ta), int(tb), m, n, k, alpha, _p(A), lda, sA, _p(B), ldb, sB, beta, _p(cin), _p(out), ldc,
+                      sC, batch, _p(bias), sBias, scale_mode, _p(sa), _p(sb), ssa, ssb, j0, j1,
+                      nthreads or nthreads_default())
+    return out
+
+
+# ------------------------------------------------------------ norms / attention
+
+def rmsnorm(x, gamma, eps, nthreads=None):
+    x = np.ascontiguousarray(x, np.float32)
+    gamma = np.ascontiguousarray(gamma, np.float32)
+    rows, hidden = x.shape
+    y = np.empty((rows, hidden), np.float64)
+    rstd = np.empty(rows, np.float64)
+    _lib.ora_rmsnorm(rows, hidden, _p(x), hidden, _p(gamma), eps, _p(y), _p(rstd), nthreads or nthreads_default())
+    return y, rstd
+
+
+def layernorm(x, gamma, beta, eps, nthreads=None):
+    x = np.ascontiguousarray(x, np.float32)
+    gamma = np.ascontiguousarray(gamma, np.float32)
+    beta = None if beta is None else np.ascontiguousarray(beta, np.float32)
+    rows, hidden = x.shape
+    y = np.empty((rows, hidden), np.float64)
+    mean = np.empty(rows, np.float64)
+    rstd = np.empty(rows, np.float64)
+    _lib.ora_layernorm(rows, hidden, _p(x), hidden, _p(gamma), _p(beta), eps, _p(y), _p(mean), _p(rstd),
+                       nthreads or nthreads_default())
+    return y, mean, rstd
+
+
+def attention(q, k, v, scale, causal, pairs=None, q0=0, q1=None, nthreads=None):
+    """q: [BH, Sq, D], k/v: [BH, Sk, D] float arrays. Returns (o [P, nq, D], lse [P, nq])."""
+    q = np.ascontiguousarray(q, np.float32)
+    k = np.ascontiguousarray(k, np.float32)
+    v = np.ascontiguousarray(v, np.float32)
+    BH, Sq, D = q.shape
+    Sk = k.shape[1]
+    pairs = np.arange(BH, dtype=np.int32) if pairs is None else np.ascontiguousarray(pairs, np.int32)
+    q1 = Sq if q1 is None else q1
+    nq = q1 - q0
+    o = np.empty((len(pairs), nq, D), np.float64)
+    lse = np.empty((len(pairs), nq), np.float64)
+    _lib.ora_attention(BH, Sq, Sk, D, _p(q), _p(k), _p(v), scale, int(causal), _p(pairs), len(pairs), q0, q1, _p(o),
+                       _p(lse), nthreads or nthreads_default())
+    return o, lse
