@@ -1,0 +1,512 @@
+"""Benchmark of the grxcp-b200 hot path on B200.
+
+Headline: grxblasGemmEx bf16 x bf16 -> fp32 accumulate ->
+bf16, M = N = K = 8192, plus a bias[N] epilogue, alpha = 1, beta = 0, called
+through the library's C-ABI. One step = one GEMM over the whole job. At N GPUs
+the GEMM is column-sharded over N (each rank owns N/G contiguous columns of B
+and C, no collective on the data path), so the total work is fixed: strong
+scaling. `value` = whole-job TFLOP/s from the max over ranks of the
+CUDA-event time of K steps.
+
+Also reported on the same line: the other BASELINE configs measured on rank 0
+(attention, RMSNorm / LayerNorm, fp8 strided-batched MLP GEMM, int8 512^3),
+the end-to-end number through the public API with host buffers, the roofline
+of the dominant kernel, clocks sampled during the timed region, and the CPU
+baseline (the oracle port of the reference's CPU GEMM loop).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+M = N = K = 8192
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.p.terminate()
+        try:
+            self.p.wait(timeout=5)
+        except Exception:
+            self.p.kill()
+        self.f.seek(0)
+        rows = [l.split(",") for l in self.f.read().splitlines() if l.strip()]
+        os.unlink(self.f.name)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                mx = float(r[2])
+                for nm, v in zip(names, r[5:9]):
+                    if v.strip().lower() == "active":
+                        reasons.add(nm)
+            except (ValueError, IndexError):
+                continue
+        loaded = [s for s in sm if mx and s > 0.5 * mx] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": mx,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle port)
+
+def cpu_gemm_sample(seconds: float, threads: int):
+    """Times the oracle port of the reference's CPU GEMM loop (tests/libs/test_grxblas.cpp:63-80:
+    naive triple loop, fp64 accumulate) on a column sample of the 8192^3 config.
+    Returns (TFLOP/s, columns, seconds)."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(0)
+    A = (rng.standard_normal(M * K, dtype=np.float32) / math.sqrt(K)).astype(np.float32)
+    cols = max(threads, 1)
+    Bs = (rng.standard_normal(K * cols, dtype=np.float32) / math.sqrt(K)).astype(np.float32)
+    out = np.empty(M * cols)
+    t0 = time.perf_counter()
+    oracle.gemm_f64(1, 0, M, cols, K, 1.0, A, K, Bs, K, out=out, nthreads=threads)
+    t1 = time.perf_counter() - t0
+    target = max(cols, int(cols * seconds / max(t1, 1e-3)))
+    target = min(target, N)
+    Bs = (rng.standard_normal(K * target, dtype=np.float32) / math.sqrt(K)).astype(np.float32)
+    out = np.empty(M * target)
+    t0 = time.perf_counter()
+    oracle.gemm_f64(1, 0, M, target, K, 1.0, A, K, Bs, K, out=out, nthreads=threads)
+    dt = time.perf_counter() - t0
+    return 2.0 * M * K * target / dt / 1e12, target, dt
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    threads = len(os.sched_getaffinity(0))
+    vals = []
+    cols = 0
+    for s in range(args.warmup + args.steps):
+        v, cols, dt = cpu_gemm_sample(2.0, threads)
+        if s >= args.warmup:
+            vals.append(v)
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference",
+        "metric": "GEMM TFLOP/s (% dense tensor peak) at 1/2/4/8 B200; attention TFLOP/s; norm GB/s",
+        "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic: A, B ~N(0,1)/sqrt(K), seeded",
+        "config": config_dict(args.gpus),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{cols} of {N} output columns of the 8192^3 GEMM per step (fp64 naive loop, "
+                                   "oracle restatement of tests/libs/test_grxblas.cpp:63-80)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(gpus):
+    return {"workload": "grxblasGemmEx bf16 in / fp32 acc / bf16 out + bias[N], M=N=K=8192 (BASELINE config 2)",
+            "m": M, "n": N, "k": K, "transa": "T", "transb": "N", "alpha": 1.0, "beta": 0.0,
+            "parallelism": f"column-shard over N x{gpus}" if gpus > 1 else "single GPU",
+            "l2": "inputs larger than L2 (A+B+C = 384 MiB per step)"}
+
+
+# ------------------------------------------------------------------ GPU arm
+
+def run_gpu(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+    from grxcp_b200 import _native as Nn
+    from grxcp_b200 import blas as B
+
+    peaks, peaks_src = load_peaks()
+    stream = torch.cuda.current_stream()
+    h = B.Handle()
+    B.check(h.set_stream(stream), "set_stream")
+
+    # column shard of B / C / bias owned by this rank
+    assert N % world == 0
+    nl = N // world
+    g = torch.Generator(device=dev).manual_seed(1234)
+    A = (torch.randn(M, K, device=dev, generator=g) / math.sqrt(K)).to(torch.bfloat16)  # stored k x m (OP_T)
+    Bfull = torch.empty(N, K, device=dev, dtype=torch.bfloat16)
+    Bfull.copy_((torch.randn(N, K, device=dev, generator=g) / math.sqrt(K)).to(torch.bfloat16))
+    Bl = Bfull[rank * nl:(rank + 1) * nl].contiguous()  # stored k x nl, column-major
+    del Bfull
+    bias = (torch.randn(N, device=dev, generator=g) * 0.02)[rank * nl:(rank + 1) * nl].contiguous()
+    C = torch.empty(nl, M, device=dev, dtype=torch.bfloat16)  # column-major m x nl
+    B.check(h.set_epilogue(bias=bias, bias_type=Nn.GRX_R_32F), "set_epilogue")
+
+    def step():
+        s = h.gemm_ex(Nn.OP_T, Nn.OP_N, M, nl, K, 1.0, A, Nn.GRX_R_16BF, K, Bl, Nn.GRX_R_16BF, K, 0.0, C,
+                      Nn.GRX_R_16BF, M)
+        if s != Nn.SUCCESS:
+            raise RuntimeError(f"grxblasGemmEx: {Nn.STATUS[s]}")
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        import torch.distributed as dist
+
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    time.sleep(0.3)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    barrier()
+    torch.cuda.synchronize()
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ms_local)
+    flops_total = 2.0 * M * N * K
+    value = flops_total / (ms * 1e-3) / 1e12
+    st = h.execution_status()
+    if st != Nn.SUCCESS:
+        raise RuntimeError(f"kernel reported {Nn.STATUS[st]}")
+
+    # per-launch kernel time of the dominant kernel = the step (one launch per step)
+    per_launch_flops = 2.0 * M * nl * K
+    achieved = per_launch_flops / (ms_local * 1e-3) / 1e12
+    peak = peaks["bf16_tflops"]
+    traffic = None
+    tr = ROOT / "profiles" / "traffic.txt"
+    if tr.exists():
+        for line in tr.read_text().splitlines():
+            parts = line.split()
+            if len(parts) == 2 and parts[0] == "gemm_bf16_8192_per_launch_bytes":
+                traffic = float(parts[1]) * nl / N  # scales with the column shard
+    roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": traffic, "peak_source": f"{peaks_src} bf16_tflops (burst)",
+                "kernel": "grx::tc_gemm_kernel<bf16, bf16 out>"}
+
+    # ---- end to end through the public API with host buffers (pinned)
+    hA = A.cpu().pin_memory()
+    hB = Bl.cpu().pin_memory()
+    hbias = bias.cpu().pin_memory()
+    hC = torch.empty(nl, M, dtype=torch.bfloat16).pin_memory()
+    dA, dB, dbias = torch.empty_like(A), torch.empty_like(Bl), torch.empty_like(bias)
+    B.check(h.set_epilogue(bias=dbias, bias_type=Nn.GRX_R_32F), "set_epilogue")
+
+    def e2e_step():
+        dA.copy_(hA, non_blocking=True)
+        dB.copy_(hB, non_blocking=True)
+        dbias.copy_(hbias, non_blocking=True)
+        s = h.gemm_ex(Nn.OP_T, Nn.OP_N, M, nl, K, 1.0, dA, Nn.GRX_R_16BF, K, dB, Nn.GRX_R_16BF, K, 0.0, C,
+                      Nn.GRX_R_16BF, M)
+        if s != Nn.SUCCESS:
+            raise RuntimeError(Nn.STATUS[s])
+        hC.copy_(C, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    h2d = (A.numel() + Bl.numel()) * 2 + bias.numel() * 4
+    d2h = C.numel() * 2
+    e2e = {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
+           "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms,
+           "note": "H2D of A, this rank's B columns and bias from pinned memory, GEMM, D2H of C, every step"}
+    del hA, hB, hC, dA, dB
+    h.clear_epilogue()
+
+    secondary = {}
+    cpu = None
+    if rank == 0:
+        if not args.no_secondary:
+            del A, Bl, C
+            torch.cuda.empty_cache()
+            secondary = run_secondary(args, peaks, dev, stream)
+        threads = len(os.sched_getaffinity(0))
+        v, cols, dt = cpu_gemm_sample(args.cpu_seconds, threads)
+        cpu = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+               "sample": f"{cols} of {N} output columns of the 8192^3 GEMM ({dt:.1f} s, fp64 naive loop, oracle "
+                         "restatement of tests/libs/test_grxblas.cpp:63-80)"}
+    if rank == 0:
+        line = {
+            "metric": "GEMM TFLOP/s (% dense tensor peak) at 1/2/4/8 B200; attention TFLOP/s; norm GB/s",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": max(args.warmup, 3),
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: A, B ~N(0,1)/sqrt(K) bf16, bias ~N(0,0.02) fp32, seeded",
+            "config": config_dict(world),
+            "frac_of_peak": value / (peak * world),
+            "roofline": roofline, "clocks": clk, "e2e": e2e, "gpu_launches": args.steps,
+            "cpu_baseline": cpu, "secondary": secondary,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def _time(fn, iters, stream):
+    import torch
+
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(iters):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def run_secondary(args, peaks, dev, stream):
+    """The other BASELINE configs on rank 0, each timed with CUDA events (inputs larger than L2)."""
+    import torch
+
+    from grxcp_b200 import _native as Nn
+    from grxcp_b200 import blas as B
+    from grxcp_b200 import dnn as D
+
+    out = {}
+    dh = D.Handle()
+    dh.set_stream(stream)
+    bh = B.Handle()
+    bh.set_stream(stream)
+    g = torch.Generator(device=dev).manual_seed(7)
+    hbm = peaks["hbm_gbs"]
+    bf16_peak = peaks["bf16_tflops"]
+
+    # config 3: RMSNorm / LayerNorm [65536, 8192] bf16
+    x = torch.randn(65536, 8192, device=dev, generator=g).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    gamma = 1 + 0.02 * torch.randn(8192, device=dev, generator=g)
+    beta = 0.02 * torch.randn(8192, device=dev, generator=g)
+    nbytes = 2 * x.numel() * 2 + 8192 * 4
+    ms = _time(lambda: dh.rmsnorm(x, gamma, 1e-5, y), 20, stream)
+    out["rmsnorm"] = {"value": nbytes / ms / 1e6, "unit": "GB/s", "ms": ms, "frac": nbytes / ms / 1e6 / hbm,
+                      "config": "bf16 [65536, 8192], fp32 gamma, eps 1e-5"}
+    ms = _time(lambda: dh.layernorm(x, gamma, beta, 1e-5, y), 20, stream)
+    nb = nbytes + 8192 * 4
+    out["layernorm"] = {"value": nb / ms / 1e6, "unit": "GB/s", "ms": ms, "frac": nb / ms / 1e6 / hbm,
+                        "config": "bf16 [65536, 8192], fp32 gamma/beta, eps 1e-5"}
+    del x, y
+    torch.cuda.empty_cache()
+
+    # config 4: causal attention B=8 H=32 S=4096 D=128
+    q = torch.randn(8, 32, 4096, 128, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn_like(q)
+    v = torch.randn_like(q)
+    o = torch.empty_like(q)
+    lse = torch.empty(8, 32, 4096, device=dev)
+    fl = 2.0 * 8 * 32 * 4096 * 4096 * 128
+    ms = _time(lambda: dh.attention(q, k, v, o, 1 / math.sqrt(128), True, lse), 10, stream)
+    out["attention"] = {"value": fl / ms / 1e9, "unit": "TFLOP/s", "ms": ms, "frac": fl / ms / 1e9 / bf16_peak,
+                        "config": "causal, bf16, B=8 H=32 S=4096 D=128, fp32 LSE; FLOP = 2*B*H*S^2*D"}
+    del q, k, v, o, lse
+    torch.cuda.empty_cache()
+
+    # config 5: fp8 e4m3 strided-batched MLP GEMM, batch 16, 4096 x 14336 x 4096, per-tensor scales, bf16 out
+    bt, m5, n5, k5 = 16, 4096, 14336, 4096
+    a8 = (torch.randn(bt, m5, k5, device=dev, generator=g)).to(torch.float8_e4m3fn)
+    b8 = (torch.randn(bt, n5, k5, device=dev, generator=g)).to(torch.float8_e4m3fn)
+    c5 = torch.empty(bt, n5, m5, device=dev, dtype=torch.bfloat16)
+    sa = torch.full((bt,), 1 / 448.0, device=dev)
+    sb = torch.full((bt,), 1 / 448.0, device=dev)
+    bh.set_epilogue(scale_mode=Nn.SCALE_TENSOR, scale_a=sa, scale_b=sb, stride_scale_a=1, stride_scale_b=1)
+    fl5 = 2.0 * bt * m5 * n5 * k5
+    ms = _time(lambda: bh.gemm_strided_batched_ex(Nn.OP_T, Nn.OP_N, m5, n5, k5, 1.0, a8, Nn.GRX_R_8F_E4M3, k5,
+                                                  m5 * k5, b8, Nn.GRX_R_8F_E4M3, k5, n5 * k5, 0.0, c5,
+                                                  Nn.GRX_R_16BF, m5, m5 * n5, bt), 5, stream)
+    fp8_peak = 2 * bf16_peak
+    out["fp8_batched_gemm"] = {"value": fl5 / ms / 1e9, "unit": "TFLOP/s", "ms": ms,
+                               "frac": fl5 / ms / 1e9 / fp8_peak,
+                               "peak_note": "fp8 peak taken as 2x the measured bf16 peak",
+                               "config": "e4m3, batch 16, 4096x14336x4096, per-tensor scales, bf16 out"}
+    # int8 variant with per-row / per-column scales
+    i8a = a8.view(torch.int8)
+    i8b = b8.view(torch.int8)
+    sra = torch.full((m5,), 0.01, device=dev)
+    srb = torch.full((n5,), 0.01, device=dev)
+    bh.set_epilogue(scale_mode=Nn.SCALE_ROWCOL, scale_a=sra, scale_b=srb)
+    ms = _time(lambda: bh.gemm_strided_batched_ex(Nn.OP_T, Nn.OP_N, m5, n5, k5, 1.0, i8a, Nn.GRX_R_8I, k5,
+                                                  m5 * k5, i8b, Nn.GRX_R_8I, k5, n5 * k5, 0.0, c5,
+                                                  Nn.GRX_R_16BF, m5, m5 * n5, bt), 5, stream)
+    out["int8_rowcol_batched_gemm"] = {"value": fl5 / ms / 1e9, "unit": "TOP/s", "ms": ms,
+                                       "frac": fl5 / ms / 1e9 / fp8_peak,
+                                       "config": "int8, batch 16, 4096x14336x4096, per-row/col scales, bf16 out"}
+    bh.clear_epilogue()
+    del a8, b8, c5
+    torch.cuda.empty_cache()
+
+    # config 1: fp32 SGEMM 512^3 and int8 512^3
+    a = torch.rand(512 * 512, device=dev, generator=g) * 2 - 1
+    b = torch.rand(512 * 512, device=dev, generator=g) * 2 - 1
+    c = torch.empty(512 * 512, device=dev)
+    ms = _time(lambda: bh.sgemm(0, 0, 512, 512, 512, 1.0, b, 512, a, 512, 0.0, c, 512), 50, stream)
+    out["sgemm_512"] = {"value": 2 * 512 ** 3 / ms / 1e9, "unit": "TFLOP/s", "ms": ms,
+                        "config": "fp32 row-major 512^3 via swapped column-major call"}
+    ia = torch.randint(-128, 128, (512 * 512,), device=dev, dtype=torch.int8)
+    ic = torch.empty(512 * 512, device=dev, dtype=torch.int32)
+    ms = _time(lambda: bh.gemm_ex(0, 0, 512, 512, 512, 1.0, ia, Nn.GRX_R_8I, 512, ia, Nn.GRX_R_8I, 512, 0.0, ic,
+                                  Nn.GRX_R_32I, 512), 50, stream)
+    out["int8_512"] = {"value": 2 * 512 ** 3 / ms / 1e9, "unit": "TOP/s", "ms": ms,
+                       "config": "int8 512^3 -> int32, bit-exact path"}
+    if dh.execution_status() != Nn.SUCCESS or bh.execution_status() != Nn.SUCCESS:
+        out["error"] = "a kernel reported a bounded-wait timeout"
+    return out
+
+
+def run_profile(args):
+    """One workload, warmup + steps launches, nothing else: the command ncu captures."""
+    import torch
+
+    from grxcp_b200 import _native as Nn
+    from grxcp_b200 import blas as B
+    from grxcp_b200 import dnn as D
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(1)
+    n_iter = args.warmup + args.steps
+    if args.profile in ("gemm", "fp8"):
+        h = B.Handle()
+        if args.profile == "gemm":
+            A = (torch.randn(M, K, device=dev, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+            Bm = (torch.randn(N, K, device=dev, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+            C = torch.empty(N, M, device=dev, dtype=torch.bfloat16)
+            bias = torch.randn(N, device=dev, generator=g) * 0.02
+            h.set_epilogue(bias=bias, bias_type=Nn.GRX_R_32F)
+            for _ in range(n_iter):
+                B.check(h.gemm_ex(1, 0, M, N, K, 1.0, A, Nn.GRX_R_16BF, K, Bm, Nn.GRX_R_16BF, K, 0.0, C,
+                                  Nn.GRX_R_16BF, M))
+        else:
+            bt, m5, n5, k5 = 16, 4096, 14336, 4096
+            a8 = torch.randn(bt, m5, k5, device=dev, generator=g).to(torch.float8_e4m3fn)
+            b8 = torch.randn(bt, n5, k5, device=dev, generator=g).to(torch.float8_e4m3fn)
+            c5 = torch.empty(bt, n5, m5, device=dev, dtype=torch.bfloat16)
+            s = torch.full((bt,), 1 / 448.0, device=dev)
+            h.set_epilogue(scale_mode=Nn.SCALE_TENSOR, scale_a=s, scale_b=s, stride_scale_a=1, stride_scale_b=1)
+            for _ in range(n_iter):
+                B.check(h.gemm_strided_batched_ex(1, 0, m5, n5, k5, 1.0, a8, Nn.GRX_R_8F_E4M3, k5, m5 * k5, b8,
+                                                  Nn.GRX_R_8F_E4M3, k5, n5 * k5, 0.0, c5, Nn.GRX_R_16BF, m5,
+                                                  m5 * n5, bt))
+        torch.cuda.synchronize()
+        B.check(h.execution_status())
+    else:
+        dh = D.Handle()
+        if args.profile == "attention":
+            q = torch.randn(8, 32, 4096, 128, device=dev, generator=g).to(torch.bfloat16)
+            k, v, o = torch.randn_like(q), torch.randn_like(q), torch.empty_like(q)
+            lse = torch.empty(8, 32, 4096, device=dev)
+            for _ in range(n_iter):
+                D.check(dh.attention(q, k, v, o, 1 / math.sqrt(128), True, lse))
+        else:
+            x = torch.randn(65536, 8192, device=dev, generator=g).to(torch.bfloat16)
+            y = torch.empty_like(x)
+            gamma = torch.ones(8192, device=dev)
+            beta = torch.zeros(8192, device=dev)
+            for _ in range(n_iter):
+                if args.profile == "rmsnorm":
+                    D.check(dh.rmsnorm(x, gamma, 1e-5, y))
+                else:
+                    D.check(dh.layernorm(x, gamma, beta, 1e-5, y))
+        torch.cuda.synchronize()
+        D.check(dh.execution_status())
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="grxcp", choices=["grxcp", "reference"])
+    ap.add_argument("--no-secondary", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--profile", choices=["gemm", "attention", "rmsnorm", "layernorm", "fp8"],
+                    help="run only this kernel warmup+steps times (for ncu captures); prints no JSON")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    if args.profile:
+        return run_profile(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -366,7 +366,9 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
   if (p.group_m <= 0) p.group_m = 16;
   p.a_mn_major = L.a_mn_major;
   p.b_mn_major = L.b_mn_major;
-  const uint32_t cfmt = (L.out == kOutS32) ? 2u : 1u;
+  // kind::i8 accumulates in s32 only (f32 is an illegal instruction there); the
+  // epilogue converts to the requested output type.
+  const uint32_t cfmt = (L.kind == kKindI8) ? 2u : 1u;
   p.idesc = make_idesc(cfmt, (uint32_t)L.a_fmt, (uint32_t)L.a_fmt, (uint32_t)L.a_mn_major, (uint32_t)L.b_mn_major,
                        kTileM, kTileN);
   const int a_bdim = (p.batch > 1 && L.stride_a != 0) ? p.batch : 1;

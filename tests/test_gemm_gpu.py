@@ -256,7 +256,8 @@ def test_gemm_fp8_per_tensor_scale_batched(blas):
     want = oracle.gemm_f64(1, 0, m, n, k, 1.0, Ad, k, Bd, k, sA=k * m, sB=k * n, sC=m * n, batch=batch,
                            scale_mode=1, sa=sa, sb=sb, ssa=1, ssb=1)
     dC = torch.full((batch * m * n,), float("nan"), dtype=torch.bfloat16, device="cuda")
-    assert blas.set_epilogue(scale_mode=N.SCALE_TENSOR, scale_a=dev_f32(sa), scale_b=dev_f32(sb),
+    dsa, dsb = dev_f32(sa), dev_f32(sb)  # the handle keeps the pointers, not the tensors
+    assert blas.set_epilogue(scale_mode=N.SCALE_TENSOR, scale_a=dsa, scale_b=dsb,
                              stride_scale_a=1, stride_scale_b=1) == N.SUCCESS
     st = blas.gemm_strided_batched_ex(1, 0, m, n, k, 1.0, dev_bits(Aq), N.GRX_R_8F_E4M3, k, k * m, dev_bits(Bq),
                                       N.GRX_R_8F_E4M3, k, k * n, 0.0, dC, N.GRX_R_16BF, m, m * n, batch)
@@ -278,7 +279,8 @@ def test_gemm_int8_rowcol_scale(blas):
     want = oracle.gemm_f64(1, 0, m, n, k, 1.0, Aq.astype(np.float32).ravel(), k, Bq.astype(np.float32).ravel(), k,
                            scale_mode=2, sa=sa, sb=sb)
     dC = torch.full((m * n,), float("nan"), dtype=torch.bfloat16, device="cuda")
-    assert blas.set_epilogue(scale_mode=N.SCALE_ROWCOL, scale_a=dev_f32(sa), scale_b=dev_f32(sb)) == N.SUCCESS
+    dsa, dsb = dev_f32(sa), dev_f32(sb)  # the handle keeps the pointers, not the tensors
+    assert blas.set_epilogue(scale_mode=N.SCALE_ROWCOL, scale_a=dsa, scale_b=dsb) == N.SUCCESS
     st = blas.gemm_ex(1, 0, m, n, k, 1.0, dev_bits(Aq.ravel()), N.GRX_R_8I, k, dev_bits(Bq.ravel()), N.GRX_R_8I, k,
                       0.0, dC, N.GRX_R_16BF, m)
     assert st == N.SUCCESS
