@@ -8,7 +8,16 @@ The product is the C-ABI shared library ``libgrxcp.so`` (headers under
     grxcp_b200.dnn     grxdnn*  (RMSNorm, LayerNorm, attention forward)
     grxcp_b200.shard   column-parallel GEMM / (batch x head)-parallel attention
                        over torch.distributed ranks, optional NCCL all-gather
-"""
-from . import _native, blas, dnn  # noqa: F401
 
-__all__ = ["blas", "dnn", "_native"]
+Submodules load on first use, so ``python -m grxcp_b200.build`` works before
+the library exists.
+"""
+import importlib
+
+__all__ = ["blas", "dnn", "shard", "_native"]
+
+
+def __getattr__(name):
+    if name in __all__:
+        return importlib.import_module(f"{__name__}.{name}")
+    raise AttributeError(name)

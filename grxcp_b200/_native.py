@@ -163,6 +163,7 @@ PROTOTYPES: dict[str, tuple] = {
     "grxblasSetWorkspace": (i32, [vp, vp, sz]),
     "grxblasGetWorkspaceSize": (sz, [vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32]),
     "grxblasGetExecutionStatus": (i32, [vp]),
+    "grxblasGemmExNoAlloc": (i32, [vp, i32, i32, i32, i32, i32, fp, vp, i32, i32, vp, i32, i32, fp, vp, i32, i32, vp]),
     # grxdnn.h
     "grxdnnGetStatusString": (cp, [i32]),
     "grxdnnCreate": (i32, [C.POINTER(vp)]),

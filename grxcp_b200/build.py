@@ -32,6 +32,7 @@ SOURCES = [
     "blas_kernels.cu",
     "norm.cu",
     "attention.cu",
+    "gemm_noalloc.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

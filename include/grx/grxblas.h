@@ -206,6 +206,31 @@ size_t          grxblasGetWorkspaceSize(grxblasHandle_t handle, grxblasOperation
  * (EXECUTION_FAILED), or whether the stream reported an error. Clears the flag. */
 grxblasStatus_t grxblasGetExecutionStatus(grxblasHandle_t handle);
 
+/* No counterpart in the reference. grxblasGemmEx for callers that may not
+ * allocate device memory -- code whose device memory is owned by another
+ * allocator (framework plug-ins, fixed-budget serving processes) or that must
+ * not trigger cudaMalloc's implicit synchronisation. Same arguments and type
+ * pairings as grxblasGemmEx, without a handle (plain alpha/beta epilogue, no
+ * bias or scales), enqueued on `stream`. It allocates nothing: operands that
+ * must be packed (address or leading dimension not 16-byte aligned) go to a
+ * fixed 16 MiB device array inside this library, which every GPU that loads the
+ * library holds until exit; a problem needing more packing scratch than that
+ * is refused with INVALID_VALUE and a stderr line. `errorFlag` is an optional
+ * device int the kernel sets non-zero if it gives up on a bounded wait. The
+ * first call on each device resolves the array's device address (make it
+ * before any stream capture). All calls share the array: calls that overlap on
+ * the GPU race and must be ordered by the caller. */
+grxblasStatus_t grxblasGemmExNoAlloc(grxStream_t stream,
+                                     grxblasOperation_t transa,
+                                     grxblasOperation_t transb,
+                                     int m, int n, int k,
+                                     const float* alpha,
+                                     const void* A, grxDataType_t Atype, int lda,
+                                     const void* B, grxDataType_t Btype, int ldb,
+                                     const float* beta,
+                                     void* C, grxDataType_t Ctype, int ldc,
+                                     int* errorFlag);
+
 #ifdef __cplusplus
 }
 #endif
