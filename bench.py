@@ -497,7 +497,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="grxcp", choices=["grxcp", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
-    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--profile", choices=["gemm", "attention", "rmsnorm", "layernorm", "fp8"],
                     help="run only this kernel warmup+steps times (for ncu captures); prints no JSON")
     args = ap.parse_args()

@@ -9,6 +9,8 @@
 // NOT_SUPPORTED (never a slower substitute).
 #include <cuda_runtime.h>
 
+#include <math.h>
+
 #include <mutex>
 
 #include "attention.cuh"
@@ -163,7 +165,7 @@ grxdnnStatus_t grxdnnAttentionForward(grxdnnHandle_t handle, const grxdnnAttnTen
   if (qd->batch != kd->batch || qd->headDim != kd->headDim) return GRXDNN_STATUS_INVALID_VALUE;
   if (qd->batch == 0 || qd->heads == 0 || qd->seq == 0) return GRXDNN_STATUS_SUCCESS;
   if (!q || !k || !v || !o) return GRXDNN_STATUS_INVALID_VALUE;
-  if (!(scale > 0.0f) && !(scale < 0.0f)) return GRXDNN_STATUS_INVALID_VALUE;
+  if (!(scale > 0.0f) || isinf(scale)) return GRXDNN_STATUS_INVALID_VALUE;  // softmax scale must be finite, > 0
   if (causal && qd->seq != kd->seq) return GRXDNN_STATUS_NOT_SUPPORTED;
   if (kd->seq == 0) return GRXDNN_STATUS_NOT_SUPPORTED;
   for (auto* d : all)

@@ -72,8 +72,8 @@ typedef struct {
  * per (batch, head). causal != 0 masks key j > query i (requires equal q/k
  * sequence lengths). dtype GRX_R_16BF (Q, K, V, O alike), headDim 128, equal
  * head counts. lse is fp32 [batch, heads, seqQ] contiguous (natural log), may
- * be NULL. The softmax runs in fp32, both contractions accumulate in fp32 on
- * the tensor cores. */
+ * be NULL. scale must be finite and > 0. The softmax runs in fp32, both
+ * contractions accumulate in fp32 on the tensor cores. */
 grxdnnStatus_t grxdnnAttentionForward(grxdnnHandle_t handle,
                                       const grxdnnAttnTensor_t* qDesc, const void* q,
                                       const grxdnnAttnTensor_t* kDesc, const void* k,
