@@ -167,7 +167,17 @@ def run_gpu(args):
     if world > 1:
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", device_id=dev)
+        # NCCL may print a banner on stdout during init; keep stdout for the JSON line.
+        sys.stdout.flush()
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", device_id=dev)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     from grxcp_b200 import _native as Nn
     from grxcp_b200 import blas as B
 
