@@ -22,6 +22,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <stdlib.h>
+
 #include <mutex>
 
 #include "gemm_tc.cuh"
@@ -67,6 +69,48 @@ __device__ __forceinline__ void store_c(void* c, long long idx, float v) {
   if constexpr (OUT == kOutF32) static_cast<float*>(c)[idx] = v;
   else if constexpr (OUT == kOutBF16) static_cast<__nv_bfloat16*>(c)[idx] = __float2bfloat16_rn(v);
   else static_cast<__half*>(c)[idx] = __float2half_rn(v);
+}
+
+// Epilogue of one output tile for the calling warp: 32 rows (thread = row i)
+// x kTileN columns from col0, read 32 columns at a time from TMEM at t_row.
+template <int KIND, int OUT>
+__device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_row, int bt, int i, int col0) {
+  const bool row_ok = i < p.m;
+  const long long cbase = (long long)bt * p.stride_c + i;
+  float rowmul = p.alpha;
+  if (p.scale_mode == 1) rowmul *= p.scale_a[bt * p.stride_sa] * p.scale_b[bt * p.stride_sb];
+  if (p.scale_mode == 2 && row_ok) rowmul *= p.scale_a[bt * p.stride_sa + i];
+  const float* sb = p.scale_b + bt * p.stride_sb;
+  const float* bias_f = static_cast<const float*>(p.bias) + bt * p.stride_bias;
+  const __nv_bfloat16* bias_h = static_cast<const __nv_bfloat16*>(p.bias) + bt * p.stride_bias;
+  for (int c0 = 0; c0 < kTileN; c0 += 32) {
+    const int jbase = col0 + c0;
+    if (jbase >= p.n) break;  // warp-uniform
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c0, r);
+    tmem_ld_wait();
+    if (row_ok) {
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj) {
+        const int j = jbase + jj;
+        if (j < p.n) {
+          const long long idx = cbase + (long long)j * p.ldc;
+          if constexpr (OUT == kOutS32) {
+            int v = p.ialpha * (int)r[jj];
+            if (p.beta_nonzero) v += p.ibeta * static_cast<const int*>(p.c)[idx];
+            static_cast<int*>(p.c)[idx] = v;
+          } else {
+            const float acc = (KIND == kKindI8) ? (float)(int)r[jj] : __uint_as_float(r[jj]);
+            float v = __fmul_rn(rowmul, acc);
+            if (p.scale_mode == 2) v = __fmul_rn(v, sb[j]);
+            if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
+            if (p.bias) v = __fadd_rn(v, p.bias_bf16 ? __bfloat162float(bias_h[j]) : bias_f[j]);
+            store_c<OUT>(p.c, idx, v);
+          }
+        }
+      }
+    }
+  }
 }
 
 template <int KIND, int OUT>
@@ -229,44 +273,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       int bt, mt, nt;
       decode_tile(p, t, bt, mt, nt);
-      const int i = mt * kTileM + row;
-      const bool row_ok = i < p.m;
-      const long long cbase = (long long)bt * p.stride_c + i;
-      float rowmul = p.alpha;
-      if (p.scale_mode == 1) rowmul *= p.scale_a[bt * p.stride_sa] * p.scale_b[bt * p.stride_sb];
-      if (p.scale_mode == 2 && row_ok) rowmul *= p.scale_a[bt * p.stride_sa + i];
-      const float* sb = p.scale_b + bt * p.stride_sb;
-      const float* bias_f = static_cast<const float*>(p.bias) + bt * p.stride_bias;
-      const __nv_bfloat16* bias_h = static_cast<const __nv_bfloat16*>(p.bias) + bt * p.stride_bias;
-      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + b * kTileN;
-      for (int c0 = 0; c0 < kTileN; c0 += 32) {
-        const int jbase = nt * kTileN + c0;
-        if (jbase >= p.n) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c0, r);
-        tmem_ld_wait();
-        if (row_ok) {
-#pragma unroll
-          for (int jj = 0; jj < 32; ++jj) {
-            const int j = jbase + jj;
-            if (j < p.n) {
-              const long long idx = cbase + (long long)j * p.ldc;
-              if constexpr (OUT == kOutS32) {
-                int v = p.ialpha * (int)r[jj];
-                if (p.beta_nonzero) v += p.ibeta * static_cast<const int*>(p.c)[idx];
-                static_cast<int*>(p.c)[idx] = v;
-              } else {
-                const float acc = (KIND == kKindI8) ? (float)(int)r[jj] : __uint_as_float(r[jj]);
-                float v = __fmul_rn(rowmul, acc);
-                if (p.scale_mode == 2) v = __fmul_rn(v, sb[j]);
-                if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
-                if (p.bias) v = __fadd_rn(v, p.bias_bf16 ? __bfloat162float(bias_h[j]) : bias_f[j]);
-                store_c<OUT>(p.c, idx, v);
-              }
-            }
-          }
-        }
-      }
+      epilogue_tile<KIND, OUT>(p, tmem_base + ((uint32_t)(q * 32) << 16) + b * kTileN, bt, mt * kTileM + row,
+                               nt * kTileN);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -278,6 +286,203 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * kTileN);
+  }
+}
+
+// CTA-pair kernel. Cluster of two CTAs (rank 0 = leader). Each CTA:
+//   warp 0      streams its 128 rows of A and its 128 columns of B per k-slab
+//               into its own kPairStages-deep ring; completion bytes of both
+//               CTAs are counted on the leader's full barrier.
+//   warp 1      leader only: one thread issues tcgen05.mma.cta_group::2
+//               (M = 256 over both CTAs' rows, N = 256 over both CTAs' B
+//               halves), and commits each stage / accumulator to the
+//               barriers of both CTAs.
+//   warps 2..5  epilogue of this CTA's 128 rows x 256 columns from its own
+//               TMEM, then one arrival on the leader's accumulator-free barrier.
+// Per SM this halves the B bytes per FLOP of the single-CTA kernel, so the
+// same shared memory keeps the tensor pipe fed across longer L2 latency.
+template <int KIND, int OUT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ TcGemmParams p) {
+  constexpr int ES = (KIND == kKindF16) ? 2 : 1;
+  constexpr int BK = 128 / ES;
+  constexpr int UK = 32 / ES;
+  constexpr int KSUB = BK / UK;
+  constexpr int ATOM = 128 / ES;
+  constexpr uint32_t kStageTx = 2u * 2u * kPairStageBytes;  // A + B halves of both CTAs
+
+  if (p.abi_version != kTcGemmAbi) {
+    if (threadIdx.x == 0 && p.err_word) atomicCAS(p.err_word, 0, kErrBadAbi);
+    return;  // both CTAs of every pair take this branch alike
+  }
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kPairStages * kPairStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + kPairStages * kPairStageBytes);
+  uint64_t* empty = full + kPairStages;
+  uint64_t* tfull = empty + kPairStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs (used on the leader)
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * kPairTileN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers initialised before any cross-CTA signal
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  WaitCtx wc{p.err_word, abort_flag, p.timeout_ns};
+  const int total = p.m_tiles * p.n_tiles * p.batch;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t armed = 0, armed_par = 0;
+      bool ok = true;
+      for (int t = pair; t < total && ok; t += npairs) {
+        int bt, mt, nt;
+        decode_tile(p, t, bt, mt, nt);
+        const int ba = bt * p.a_batch_step, bb = bt * p.b_batch_step;
+        const int row0 = mt * kPairTileM + (int)rank * 128;
+        const int col0 = nt * kPairTileN + (int)rank * 128;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded(&empty[stage], phase ^ 1u, wc, kErrTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          if (leader) {
+            mbar_arrive_expect_tx(&full[stage], kStageTx);
+            armed |= 1u << stage;
+            armed_par = (armed_par & ~(1u << stage)) | (phase << stage);
+          }
+          const uint32_t fb = leader_addr(&full[stage]);
+          uint8_t* a_dst = sA + stage * kPairStageBytes;
+          uint8_t* b_dst = sB + stage * kPairStageBytes;
+          const int k0 = kb * BK;
+          if (!p.a_mn_major) {
+            tma_load_3d_pair(a_dst, &tmA, fb, k0, row0, ba);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 128 / ATOM; ++j) tma_load_3d_pair(a_dst + j * (BK * 128), &tmA, fb, row0 + j * ATOM, k0, ba);
+          }
+          if (!p.b_mn_major) {
+            tma_load_3d_pair(b_dst, &tmB, fb, k0, col0, bb);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 128 / ATOM; ++j) tma_load_3d_pair(b_dst + j * (BK * 128), &tmB, fb, col0 + j * ATOM, k0, bb);
+          }
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Both CTAs' loads complete on the leader's full barriers: after an
+      // abort the leader lets every armed stage land; the closing cluster
+      // barrier holds the peer until then.
+      if (!ok && leader) {
+        for (int s = 0; s < kPairStages; ++s)
+          if (armed & (1u << s)) wait_drain(&full[s], (armed_par >> s) & 1u, p.timeout_ns, p.err_word);
+      }
+    }
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int t = pair; t < total && ok; t += npairs, ++local) {
+        const int b = local & 1;
+        if (!wait_bounded(&tempty[b], ((local >> 1) & 1) ^ 1u, wc, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * kPairTileN;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bounded(&full[stage], phase, wc, kErrTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sA + stage * kPairStageBytes);
+          const uint32_t b_addr = smem_u32(sB + stage * kPairStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < KSUB; ++kk) {
+            const uint64_t ad = p.a_mn_major ? sw128_desc(a_addr + kk * UK * 128, BK * 128, 1024)
+                                             : sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = p.b_mn_major ? sw128_desc(b_addr + kk * UK * 128, BK * 128, 1024)
+                                             : sw128_desc(b_addr + kk * 32, 16, 1024);
+            mma_ss_pair<KIND>(d_tmem, ad, bd, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&empty[stage], 0x3);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit_pair(&tfull[b], 0x3);
+      }
+      mma_commit_pair(drain, 0x1);
+      wait_drain(drain, 0, p.timeout_ns, p.err_word);
+    }
+  } else {
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    int local = 0;
+    for (int t = pair; t < total; t += npairs, ++local) {
+      const int b = local & 1;
+      if (!wait_bounded(&tfull[b], (local >> 1) & 1, wc, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      int bt, mt, nt;
+      decode_tile(p, t, bt, mt, nt);
+      epilogue_tile<KIND, OUT>(p, tmem_base + ((uint32_t)(q * 32) << 16) + b * kPairTileN, bt,
+                               mt * kPairTileM + (int)rank * 128 + row, nt * kPairTileN);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&tempty[b]);
+        else mbar_arrive_cluster(&tempty[b], 0);
+      }
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still touch its smem or TMEM
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * kPairTileN);
   }
 }
 
@@ -355,13 +560,45 @@ static cudaError_t launch_impl(const CUtensorMap& ma, const CUtensorMap& mb, con
   return cudaGetLastError();
 }
 
+template <int KIND, int OUT>
+static cudaError_t launch_pair_impl(const CUtensorMap& ma, const CUtensorMap& mb, const TcGemmParams& p, int grid,
+                                    cudaStream_t s) {
+  auto kfn = tc_gemm_pair_kernel<KIND, OUT>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [&] {
+    attr_err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  kfn<<<grid, kGemmThreads, kPairSmem, s>>>(ma, mb, p);
+  return cudaGetLastError();
+}
+
+// Measured on B200 (8192^3): the pair kernel wins for 16-bit operands with an
+// MN-major operand (NN +8 %, NT +14 %, TT +2 %) and ties on TN; it loses for
+// 8-bit operands (the tensor pipe consumes k twice as fast there, so the
+// extra cross-CTA hand-off shows) and for problems with fewer than ~4 tiles
+// per CTA pair. GRX_GEMM_NO_PAIR=1 forces the single-CTA kernel;
+// GRX_GEMM_FORCE_PAIR=1 takes the pair kernel for every type whenever m and n
+// are at least 256 (the tests use it to cover that kernel at modest sizes).
+static bool use_pair(int kind, const TcGemmParams& p, int num_sms) {
+  if (getenv("GRX_GEMM_NO_PAIR")) return false;
+  if (getenv("GRX_GEMM_FORCE_PAIR")) return p.m >= kPairTileM && p.n >= kPairTileN;
+  if (kind != kKindF16) return false;
+  const long long tiles = (long long)((p.m + kPairTileM - 1) / kPairTileM) * ((p.n + kPairTileN - 1) / kPairTileN) *
+                          p.batch;
+  return p.m >= kPairTileM && p.n >= kPairTileN && tiles >= 4LL * (num_sms / 2);
+}
+
 cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stream) {
   const int es = L.kind == kKindF16 ? 2 : 1;
   TcGemmParams p = L.p;
   p.abi_version = kTcGemmAbi;
   const int bk = 128 / es;
-  p.m_tiles = (p.m + kTileM - 1) / kTileM;
-  p.n_tiles = (p.n + kTileN - 1) / kTileN;
+  const bool pair = use_pair(L.kind, p, num_sms);
+  const int tile_m = pair ? kPairTileM : kTileM, tile_n = pair ? kPairTileN : kTileN;
+  p.m_tiles = (p.m + tile_m - 1) / tile_m;
+  p.n_tiles = (p.n + tile_n - 1) / tile_n;
   p.k_blocks = (p.k + bk - 1) / bk;
   if (p.group_m <= 0) p.group_m = 16;
   p.a_mn_major = L.a_mn_major;
@@ -370,18 +607,35 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
   // epilogue converts to the requested output type.
   const uint32_t cfmt = (L.kind == kKindI8) ? 2u : 1u;
   p.idesc = make_idesc(cfmt, (uint32_t)L.a_fmt, (uint32_t)L.a_fmt, (uint32_t)L.a_mn_major, (uint32_t)L.b_mn_major,
-                       kTileM, kTileN);
+                       pair ? kPairTileM : kTileM, pair ? kPairTileN : kTileN);
   const int a_bdim = (p.batch > 1 && L.stride_a != 0) ? p.batch : 1;
   const int b_bdim = (p.batch > 1 && L.stride_b != 0) ? p.batch : 1;
   p.a_batch_step = a_bdim > 1 ? 1 : 0;
   p.b_batch_step = b_bdim > 1 ? 1 : 0;
   CUtensorMap ma, mb;
-  if (!make_operand_map(&ma, L.a, es, L.a_mn_major, p.m, p.k, L.lda, L.stride_a, a_bdim, kTileM))
+  // Box rows: 128 of A per CTA in both kernels; 256 (single CTA) or 128 (each
+  // CTA of a pair) of B.
+  if (!make_operand_map(&ma, L.a, es, L.a_mn_major, p.m, p.k, L.lda, L.stride_a, a_bdim, 128))
     return cudaErrorInvalidValue;
-  if (!make_operand_map(&mb, L.b, es, L.b_mn_major, p.n, p.k, L.ldb, L.stride_b, b_bdim, kTileN))
+  if (!make_operand_map(&mb, L.b, es, L.b_mn_major, p.n, p.k, L.ldb, L.stride_b, b_bdim, pair ? 128 : kTileN))
     return cudaErrorInvalidValue;
   const long long tiles = (long long)p.m_tiles * p.n_tiles * p.batch;
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (pair) {
+    const int pairs = (int)(tiles < num_sms / 2 ? tiles : num_sms / 2);
+    const int g2 = 2 * pairs;
+    switch (L.kind * 4 + L.out) {
+      case kKindF16 * 4 + kOutF32: return launch_pair_impl<kKindF16, kOutF32>(ma, mb, p, g2, stream);
+      case kKindF16 * 4 + kOutBF16: return launch_pair_impl<kKindF16, kOutBF16>(ma, mb, p, g2, stream);
+      case kKindF16 * 4 + kOutF16: return launch_pair_impl<kKindF16, kOutF16>(ma, mb, p, g2, stream);
+      case kKindI8 * 4 + kOutS32: return launch_pair_impl<kKindI8, kOutS32>(ma, mb, p, g2, stream);
+      case kKindI8 * 4 + kOutBF16: return launch_pair_impl<kKindI8, kOutBF16>(ma, mb, p, g2, stream);
+      case kKindI8 * 4 + kOutF32: return launch_pair_impl<kKindI8, kOutF32>(ma, mb, p, g2, stream);
+      case kKindF8 * 4 + kOutBF16: return launch_pair_impl<kKindF8, kOutBF16>(ma, mb, p, g2, stream);
+      case kKindF8 * 4 + kOutF32: return launch_pair_impl<kKindF8, kOutF32>(ma, mb, p, g2, stream);
+      default: return cudaErrorNotSupported;
+    }
+  }
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
   switch (L.kind * 4 + L.out) {
     case kKindF16 * 4 + kOutF32: return launch_impl<kKindF16, kOutF32>(ma, mb, p, grid, stream);

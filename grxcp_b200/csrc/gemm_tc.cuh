@@ -59,6 +59,14 @@ constexpr int kStageBytesB = kTileN * 128;
 constexpr int kGemmThreads = 192;             // 6 warps: TMA, MMA, 4 x epilogue
 constexpr int kGemmSmem = kStages * (kStageBytesA + kStageBytesB) + 1024 /*align*/ + 256 /*barriers*/;
 
+// CTA-pair (cta_group::2) variant: a cluster of 2 CTAs computes a 256 x 256
+// tile; each CTA stages 128 rows of A and 128 columns of B per k-slab.
+constexpr int kPairTileM = 256;
+constexpr int kPairTileN = 256;
+constexpr int kPairStages = 6;
+constexpr int kPairStageBytes = 128 * 128;  // one operand half, 128 bytes of k per row
+constexpr int kPairSmem = kPairStages * 2 * kPairStageBytes + 1024 + 256;
+
 // Enqueues the kernel (builds the TMA tensor maps). Returns cudaErrorInvalidValue
 // when an operand does not meet TMA alignment (the caller packs it first).
 cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stream);

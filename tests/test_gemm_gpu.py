@@ -328,3 +328,68 @@ def test_gemm_refusals_on_device(blas):
     # mixed 16-bit input types
     assert blas.gemm_ex(0, 0, 8, 4, 8, one, d, N.GRX_R_16F, 8, d, N.GRX_R_16BF, 8, 0.0, d, N.GRX_R_32F, 8) == \
         N.NOT_SUPPORTED
+
+
+# ------------------------------------------------------------------ CTA-pair path (forced for every type)
+
+@pytest.mark.parametrize("ta,tb", [(1, 0), (0, 0), (0, 1), (1, 1)])
+def test_pair_path_bf16_bias_ragged(blas, ta, tb, monkeypatch):
+    monkeypatch.setenv("GRX_GEMM_FORCE_PAIR", "1")
+    """Problems large enough for the cta_group::2 kernel (256 x 256 tiles over CTA pairs),
+    every transpose, ragged m and n (edge tiles of both CTAs of a pair)."""
+    m, n, k = 2600, 2100, 320
+    A, B, bias = _bf16_problem(m, n, k, 17)
+    lda, ldb = (k if ta else m), (n if tb else k)
+    want = oracle.gemm_f64(ta, tb, m, n, k, 1.0, A, lda, B, ldb, bias=bias)
+    dC = torch.full((m * n,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    dbias = dev_f32(bias)
+    assert blas.set_epilogue(bias=dbias, bias_type=N.GRX_R_32F) == N.SUCCESS
+    st = blas.gemm_ex(ta, tb, m, n, k, 1.0, dev_bits(oracle.encode("bf16", A)), N.GRX_R_16BF, lda,
+                      dev_bits(oracle.encode("bf16", B)), N.GRX_R_16BF, ldb, 0.0, dC, N.GRX_R_16BF, m)
+    assert st == N.SUCCESS
+    torch.cuda.synchronize()
+    assert blas.execution_status() == N.SUCCESS
+    ok, nbad = close(dC.float().cpu().numpy(), want)
+    assert ok, f"{nbad} elements out of tolerance"
+
+
+@pytest.mark.parametrize("ta,tb", [(1, 0), (0, 1)])
+def test_pair_path_int8_exact_with_beta(blas, ta, tb, monkeypatch):
+    monkeypatch.setenv("GRX_GEMM_FORCE_PAIR", "1")
+    m, n, k, pad = 2560, 2048, 256, 16
+    a_rows, a_cols = (k, m) if ta else (m, k)
+    b_rows, b_cols = (n, k) if tb else (k, n)
+    lda, ldb, ldc = a_rows + pad, b_rows + pad, m + pad
+    A, B, C = int8_patterns(lda * a_cols, ldb * b_cols, ldc * n)
+    want = oracle.igemm(ta, tb, m, n, k, 3, A, lda, B, ldb, -2, C, ldc)
+    dC = torch.from_numpy(C.copy()).cuda()
+    st = blas.gemm_ex(ta, tb, m, n, k, 3.0, dev_bits(A), N.GRX_R_8I, lda, dev_bits(B), N.GRX_R_8I, ldb, -2.0, dC,
+                      N.GRX_R_32I, ldc)
+    assert st == N.SUCCESS
+    torch.cuda.synchronize()
+    assert np.array_equal(dC.cpu().numpy(), want)
+
+
+def test_pair_path_fp8_batched_scaled(blas, monkeypatch):
+    monkeypatch.setenv("GRX_GEMM_FORCE_PAIR", "1")
+    batch, m, n, k = 4, 1024, 1536, 384
+    rng = np.random.default_rng(29)
+    Af = rng.standard_normal((batch, m, k)).astype(np.float32)  # OP_T: stored k x m
+    Bf = rng.standard_normal((batch, n, k)).astype(np.float32)
+    sa = (np.abs(Af).reshape(batch, -1).max(1) / 448).astype(np.float32)
+    sb = (np.abs(Bf).reshape(batch, -1).max(1) / 448).astype(np.float32)
+    Aq = oracle.encode("e4m3", Af / sa[:, None, None])
+    Bq = oracle.encode("e4m3", Bf / sb[:, None, None])
+    want = oracle.gemm_f64(1, 0, m, n, k, 1.0, oracle.decode("e4m3", Aq).ravel(), k,
+                           oracle.decode("e4m3", Bq).ravel(), k, sA=k * m, sB=k * n, sC=m * n, batch=batch,
+                           scale_mode=1, sa=sa, sb=sb, ssa=1, ssb=1)
+    dC = torch.full((batch * m * n,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    dsa, dsb = dev_f32(sa), dev_f32(sb)
+    assert blas.set_epilogue(scale_mode=N.SCALE_TENSOR, scale_a=dsa, scale_b=dsb, stride_scale_a=1,
+                             stride_scale_b=1) == N.SUCCESS
+    st = blas.gemm_strided_batched_ex(1, 0, m, n, k, 1.0, dev_bits(Aq), N.GRX_R_8F_E4M3, k, k * m, dev_bits(Bq),
+                                      N.GRX_R_8F_E4M3, k, k * n, 0.0, dC, N.GRX_R_16BF, m, m * n, batch)
+    assert st == N.SUCCESS
+    torch.cuda.synchronize()
+    ok, nbad = close(dC.float().cpu().numpy(), want)
+    assert ok, nbad
