@@ -83,9 +83,8 @@ struct WaitCtx {
 // Waits for the phase of `bar` with the given parity. Returns false when the
 // wait was abandoned: on timeout (recording `code`) or because another role of
 // this CTA already aborted.
-static __device__ __noinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const WaitCtx& w, int code) {
+static __device__ __noinline__ bool wait_bounded_slow(uint64_t* bar, uint32_t parity, const WaitCtx& w, int code) {
   const uint32_t addr = smem_u32(bar);
-  if (mbar_try_wait(addr, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(addr, parity)) return true;
@@ -98,6 +97,14 @@ static __device__ __noinline__ bool wait_bounded(uint64_t* bar, uint32_t parity,
       }
     }
   }
+}
+
+// Inline first probe; only a barrier that is not yet complete pays for the
+// out-of-line bounded loop (whose call would otherwise make every caller
+// spill around it).
+__device__ __forceinline__ bool wait_bounded(uint64_t* bar, uint32_t parity, const WaitCtx& w, int code) {
+  if (mbar_try_wait(smem_u32(bar), parity)) return true;
+  return wait_bounded_slow(bar, parity, w, code);
 }
 
 // ---------------------------------------------------------------- TMA
