@@ -66,6 +66,9 @@ _protos = {
     "ora_rmsnorm": (None, [_i, _i, _vp, _ll, _vp, _d, _vp, _vp, _i]),
     "ora_layernorm": (None, [_i, _i, _vp, _ll, _vp, _vp, _d, _vp, _vp, _vp, _i]),
     "ora_attention": (None, [_i, _i, _i, _i, _vp, _vp, _vp, _d, _i, _vp, _i, _i, _i, _vp, _vp, _i]),
+    "ora_saxpy": (None, [_i, _f, _vp, _i, _vp, _i]),
+    "ora_sscal": (None, [_i, _f, _vp, _i]),
+    "ora_sgemv": (None, [_i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
 }
 for _n, (_r, _a) in _protos.items():
     getattr(_lib, _n).restype = _r
@@ -209,3 +212,27 @@ def attention(q, k, v, scale, causal, pairs=None, q0=0, q1=None, nthreads=None):
     _lib.ora_attention(BH, Sq, Sk, D, _p(q), _p(k), _p(v), scale, int(causal), _p(pairs), len(pairs), q0, q1, _p(o),
                        _p(lse), nthreads or nthreads_default())
     return o, lse
+
+
+# ------------------------------------------------------------ level 1 / 2
+
+def saxpy(n, alpha, x, incx, y, incy):
+    """tests/libs/test_grxblas_l12.cpp:79-92; returns the new y buffer."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.array(y, dtype=np.float32, copy=True)
+    _lib.ora_saxpy(n, alpha, _p(x), incx, _p(out), incy)
+    return out
+
+
+def sscal(n, alpha, x, incx):
+    out = np.array(x, dtype=np.float32, copy=True)
+    _lib.ora_sscal(n, alpha, _p(out), incx)
+    return out
+
+
+def sgemv(trans, m, n, alpha, A, lda, x, incx, beta, y, incy):
+    A = np.ascontiguousarray(A, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.array(y, dtype=np.float32, copy=True)
+    _lib.ora_sgemv(int(trans), m, n, alpha, _p(A), lda, _p(x), incx, beta, _p(out), incy)
+    return out

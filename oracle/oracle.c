@@ -12,6 +12,7 @@
  *   ora_gemm_f32seq   tests/libs/test_grxblas_ex.cpp:45-63   fp16 GemmEx gate (exact inputs)
  *   ora_igemm         tests/libs/test_grxblas_ex.cpp:267-281 int8 -> int32 gate
  *   ora_igemm_npu     tests/libs/test_grxblas_npu.cpp:50-66  int8, int64 accumulate, row-major
+ *   ora_saxpy / ora_sscal / ora_sgemv  tests/libs/test_grxblas_l12.cpp:79-175 (level 1/2)
  *   ora_gemm_f64      fp64 GEMM + epilogue (bias, scales, beta) for bf16/fp8/int8-scaled
  *                     GemmEx (no reference code: parity unpinned by the reference)
  *   ora_rmsnorm / ora_layernorm / ora_attention   fp64 definitions (grxDNN is planned only
@@ -427,4 +428,45 @@ void ora_attention(int BH, int Sq, int Sk, int D, const float* q, const float* k
     for (int t = 0; t < nthreads; ++t) pthread_join(th[t], 0);
   free(jobs);
   free(th);
+}
+
+/* ------------------------------------------------------------ level 1 / 2 */
+
+/* BLAS increment addressing (tests/libs/test_grxblas_l12.cpp:27-31). */
+static long long ora_vec_index(long long i, long long n, int inc) {
+  return inc > 0 ? i * inc : (n - 1 - i) * (long long)(-inc);
+}
+
+/* y = alpha*x + y (tests/libs/test_grxblas_l12.cpp:79-92) */
+void ora_saxpy(int n, float alpha, const float* x, int incx, float* y, int incy) {
+  for (int i = 0; i < n; ++i) {
+    const float t = alpha * x[ora_vec_index(i, n, incx)];
+    y[ora_vec_index(i, n, incy)] = t + y[ora_vec_index(i, n, incy)];
+  }
+}
+
+/* x = alpha*x, incx > 0 (tests/libs/test_grxblas_l12.cpp:110-117) */
+void ora_sscal(int n, float alpha, float* x, int incx) {
+  for (int i = 0; i < n; ++i) x[ora_vec_index(i, n, incx)] = alpha * x[ora_vec_index(i, n, incx)];
+}
+
+/* y = alpha*op(A)*x + beta*y, A stored m x n column-major; beta == 0 never
+ * reads y (tests/libs/test_grxblas_l12.cpp:135-175). */
+void ora_sgemv(int trans, int m, int n, float alpha, const float* A, int lda, const float* x, int incx, float beta,
+               float* y, int incy) {
+  const int rows = trans ? n : m, depth = trans ? m : n;
+  for (int o = 0; o < rows; ++o) {
+    float acc = 0.0f;
+    for (int d = 0; d < depth; ++d) {
+      const int ar = trans ? d : o, ac = trans ? o : d;
+      const float p = A[(size_t)ar + (size_t)ac * (size_t)lda] * x[ora_vec_index(d, depth, incx)];
+      acc = acc + p;
+    }
+    const long long yi = ora_vec_index(o, rows, incy);
+    if (beta == 0.0f) y[yi] = alpha * acc;
+    else {
+      const float t1 = alpha * acc, t2 = beta * y[yi];
+      y[yi] = t1 + t2;
+    }
+  }
 }
