@@ -73,8 +73,32 @@ __device__ __forceinline__ void store_c(void* c, long long idx, float v) {
 
 // Epilogue of one output tile for the calling warp: 32 rows (thread = row i)
 // x kTileN columns from col0, read 32 columns at a time from TMEM at t_row.
+//
+// Fast path (a full 32 x 32 chunk, beta == 0, C and ldc allow 2-element
+// stores): lanes 2r and 2r+1 swap one value with shfl.xor 1, so each lane
+// holds two consecutive ROWS of one column -- adjacent in column-major C --
+// and writes them with one 4-byte (16-bit C) or 8-byte (32-bit C) store; the
+// column pointer advances by ldc, with no per-element index arithmetic or
+// bounds test. Everything else (ragged edges, beta != 0) takes the
+// element-wise path, which also defines the arithmetic both paths share.
+// alpha * s(i,j) * acc, then (caller) + beta * C, then + bias[j].
+template <int KIND>
+__device__ __forceinline__ float epi_scaled(const TcGemmParams& p, uint32_t raw, float rowmul, const float* sb, int j) {
+  const float acc = (KIND == kKindI8) ? (float)(int)raw : __uint_as_float(raw);
+  float v = __fmul_rn(rowmul, acc);
+  if (p.scale_mode == 2) v = __fmul_rn(v, sb[j]);
+  return v;
+}
+__device__ __forceinline__ float epi_bias(const TcGemmParams& p, float v, const float* bias_f,
+                                          const __nv_bfloat16* bias_h, int j) {
+  if (p.bias) v = __fadd_rn(v, p.bias_bf16 ? __bfloat162float(bias_h[j]) : bias_f[j]);
+  return v;
+}
+
 template <int KIND, int OUT>
 __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_row, int bt, int i, int col0) {
+  constexpr int kOutBytes = (OUT == kOutBF16 || OUT == kOutF16) ? 2 : 4;
+  const int lane = threadIdx.x & 31;
   const bool row_ok = i < p.m;
   const long long cbase = (long long)bt * p.stride_c + i;
   float rowmul = p.alpha;
@@ -83,12 +107,65 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_
   const float* sb = p.scale_b + bt * p.stride_sb;
   const float* bias_f = static_cast<const float*>(p.bias) + bt * p.stride_bias;
   const __nv_bfloat16* bias_h = static_cast<const __nv_bfloat16*>(p.bias) + bt * p.stride_bias;
+  // Pair stores need an even row index for the even lane, an even ldc / batch
+  // stride and a C base aligned to two elements.
+  const int i_warp0 = __shfl_sync(0xffffffffu, i, 0);
+  const bool pair_ok = !p.beta_nonzero && (p.ldc % 2 == 0) && (p.stride_c % 2 == 0) && (i_warp0 % 2 == 0) &&
+                       ((reinterpret_cast<uintptr_t>(p.c) % (2 * kOutBytes)) == 0) && i_warp0 + 31 < p.m;
   for (int c0 = 0; c0 < kTileN; c0 += 32) {
     const int jbase = col0 + c0;
     if (jbase >= p.n) break;  // warp-uniform
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_row + c0, r);
     tmem_ld_wait();
+    if (pair_ok && jbase + 32 <= p.n) {
+      const bool odd = lane & 1;
+      // even lane: rows (i, i+1) of columns jbase+jj; odd lane: rows (i-1, i) of jbase+jj+1
+      const long long base = cbase - (odd ? 1 : 0) + (long long)(jbase + (odd ? 1 : 0)) * p.ldc;
+      const long long step = 2 * p.ldc;
+      if constexpr (OUT == kOutS32) {
+        int* cp = static_cast<int*>(p.c) + base;
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 2) {
+          const int a = p.ialpha * (int)r[jj], b = p.ialpha * (int)r[jj + 1];
+          const int other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
+          *reinterpret_cast<int2*>(cp) = odd ? make_int2(other, b) : make_int2(a, other);
+          cp += step;
+        }
+      } else {
+        // This chunk's 32 column scales and biases: one load per lane, then
+        // broadcast by shuffle (instead of 32 same-address loads per lane).
+        const int jl = jbase + lane;
+        const float sb_l = p.scale_mode == 2 ? sb[jl] : 1.f;
+        const float bias_l = p.bias ? (p.bias_bf16 ? __bfloat162float(bias_h[jl]) : bias_f[jl]) : 0.f;
+#pragma unroll
+        for (int jj = 0; jj < 32; jj += 2) {
+          const float acc_a = (KIND == kKindI8) ? (float)(int)r[jj] : __uint_as_float(r[jj]);
+          const float acc_b = (KIND == kKindI8) ? (float)(int)r[jj + 1] : __uint_as_float(r[jj + 1]);
+          float a = __fmul_rn(rowmul, acc_a), b = __fmul_rn(rowmul, acc_b);
+          if (p.scale_mode == 2) {
+            a = __fmul_rn(a, __shfl_sync(0xffffffffu, sb_l, jj));
+            b = __fmul_rn(b, __shfl_sync(0xffffffffu, sb_l, jj + 1));
+          }
+          if (p.bias) {
+            a = __fadd_rn(a, __shfl_sync(0xffffffffu, bias_l, jj));
+            b = __fadd_rn(b, __shfl_sync(0xffffffffu, bias_l, jj + 1));
+          }
+          const float other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
+          const float lo = odd ? other : a, hi = odd ? b : other;  // lower row first
+          const long long off = base + (long long)(jj / 2) * step;
+          if constexpr (OUT == kOutF32) {
+            *reinterpret_cast<float2*>(static_cast<float*>(p.c) + off) = make_float2(lo, hi);
+          } else if constexpr (OUT == kOutBF16) {
+            *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.c) + off) =
+                __floats2bfloat162_rn(lo, hi);
+          } else {
+            *reinterpret_cast<__half2*>(static_cast<__half*>(p.c) + off) = __floats2half2_rn(lo, hi);
+          }
+        }
+      }
+      continue;
+    }
     if (row_ok) {
 #pragma unroll
       for (int jj = 0; jj < 32; ++jj) {
@@ -100,12 +177,9 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_
             if (p.beta_nonzero) v += p.ibeta * static_cast<const int*>(p.c)[idx];
             static_cast<int*>(p.c)[idx] = v;
           } else {
-            const float acc = (KIND == kKindI8) ? (float)(int)r[jj] : __uint_as_float(r[jj]);
-            float v = __fmul_rn(rowmul, acc);
-            if (p.scale_mode == 2) v = __fmul_rn(v, sb[j]);
+            float v = epi_scaled<KIND>(p, r[jj], rowmul, sb, j);
             if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
-            if (p.bias) v = __fadd_rn(v, p.bias_bf16 ? __bfloat162float(bias_h[j]) : bias_f[j]);
-            store_c<OUT>(p.c, idx, v);
+            store_c<OUT>(p.c, idx, epi_bias(p, v, bias_f, bias_h, j));
           }
         }
       }
