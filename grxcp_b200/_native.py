@@ -44,6 +44,8 @@ class grxblasEpilogue_t(C.Structure):
         ("scaleB", vp),
         ("strideScaleA", i64),
         ("strideScaleB", i64),
+        ("biasOverRows", i32),
+        ("activation", i32),
     ]
 
 
@@ -190,6 +192,8 @@ PROTOTYPES: dict[str, tuple] = {
         ],
     ),
     "grxdnnGetExecutionStatus": (i32, [vp]),
+    "grxdnnSoftmaxForward": (i32, [vp, i32, i32, vp, i32, i64, vp, i32, i64]),
+    "grxdnnGeluForward": (i32, [vp, i64, vp, i32, vp, i32, i32]),
 }
 
 # Internal test hook (not in the public headers).
@@ -215,3 +219,4 @@ STATUS = {
 }
 SUCCESS, NOT_INITIALIZED, ALLOC_FAILED, INVALID_VALUE, ARCH_MISMATCH, EXECUTION_FAILED, NOT_SUPPORTED, INTERNAL_ERROR = range(8)
 SCALE_NONE, SCALE_TENSOR, SCALE_ROWCOL = 0, 1, 2
+ACT_NONE, ACT_RELU, ACT_GELU_TANH, ACT_GELU_ERF = 0, 1, 2, 3

@@ -99,7 +99,8 @@ class Handle:
         return s.value or 0
 
     def set_epilogue(self, bias=None, bias_type=None, stride_bias=0, scale_mode=N.SCALE_NONE, scale_a=None,
-                     scale_b=None, stride_scale_a=0, stride_scale_b=0) -> int:
+                     scale_b=None, stride_scale_a=0, stride_scale_b=0, bias_over_rows=False,
+                     activation=N.ACT_NONE) -> int:
         e = N.grxblasEpilogue_t()
         e.bias = ptr(bias)
         e.biasType = bias_type if bias_type is not None else (dtype_code(bias) if bias is not None else N.GRX_R_32F)
@@ -109,6 +110,8 @@ class Handle:
         e.scaleB = ptr(scale_b)
         e.strideScaleA = stride_scale_a
         e.strideScaleB = stride_scale_b
+        e.biasOverRows = 1 if bias_over_rows else 0
+        e.activation = activation
         return lib.grxblasSetEpilogue(self.h, C.byref(e))
 
     def clear_epilogue(self) -> int:

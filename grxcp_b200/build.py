@@ -33,6 +33,7 @@ SOURCES = [
     "norm.cu",
     "attention.cu",
     "gemm_noalloc.cu",
+    "softmax.cu",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -218,13 +218,16 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
   if (epi.scaleMode != GRXBLAS_SCALE_NONE && (!epi.scaleA || !epi.scaleB)) return GRXBLAS_STATUS_INVALID_VALUE;
   if ((unsigned)epi.scaleMode > 2u) return GRXBLAS_STATUS_INVALID_VALUE;
   if (epi.bias && epi.biasType != GRX_R_32F && epi.biasType != GRX_R_16BF) return GRXBLAS_STATUS_NOT_SUPPORTED;
+  if ((unsigned)epi.activation > 3u) return GRXBLAS_STATUS_INVALID_VALUE;
+  if (tc.out == grx::kOutS32 && ctx.has_epi && (epi.activation != GRXBLAS_ACT_NONE)) return GRXBLAS_STATUS_NOT_SUPPORTED;
   const int bias_bf16 = (epi.bias && epi.biasType == GRX_R_16BF) ? 1 : 0;
 
   if (k == 0) {
     // C = beta*C (+ bias): no product to form (reference test case "k = 0
     // scales C by beta", tests/libs/test_grxblas_ex.cpp:217).
     return from_cuda(grx::launch_gemm_k0(tc.out, C, ldc, strideC, m, n, batch, *beta, (int)*beta, epi.bias,
-                                         bias_bf16, epi.strideBias, ctx.stream));
+                                         bias_bf16, epi.strideBias, epi.biasOverRows ? 1 : 0, (int)epi.activation,
+                                         ctx.stream));
   }
 
   OperandPlan pa = plan_operand(A, ta ? 0 : 1, lda, strideA, tc.es, batch);
@@ -277,6 +280,8 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
   p.stride_c = strideC;
   p.bias = epi.bias;
   p.bias_bf16 = bias_bf16;
+  p.bias_rows = epi.biasOverRows ? 1 : 0;
+  p.act = (int)epi.activation;
   p.stride_bias = epi.strideBias;
   p.scale_mode = (int)epi.scaleMode;
   p.scale_a = epi.scaleA;
@@ -398,7 +403,8 @@ grxblasStatus_t grxblasGemmStridedBatchedEx(grxblasHandle_t handle, grxblasOpera
 grxblasStatus_t grxblasSetEpilogue(grxblasHandle_t handle, const grxblasEpilogue_t* epilogue) {
   if (!handle) return GRXBLAS_STATUS_NOT_INITIALIZED;
   auto* ctx = reinterpret_cast<grxblasContext*>(handle);
-  if (epilogue && (unsigned)epilogue->scaleMode > 2u) return GRXBLAS_STATUS_INVALID_VALUE;
+  if (epilogue && ((unsigned)epilogue->scaleMode > 2u || (unsigned)epilogue->activation > 3u))
+    return GRXBLAS_STATUS_INVALID_VALUE;
   std::lock_guard<std::mutex> lock(ctx->mutex);
   if (epilogue) {
     ctx->epi = *epilogue;

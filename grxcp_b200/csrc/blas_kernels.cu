@@ -4,6 +4,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "activation.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
 
@@ -167,7 +168,7 @@ cudaError_t launch_pack_kmajor(const void* src, int es, int src_mn_major, long l
 
 template <int OUT>
 __global__ void gemm_k0_kernel(void* c, long long ldc, long long stride_c, int m, int n, float beta, int ibeta,
-                               const void* bias, int bias_bf16, long long stride_bias) {
+                               const void* bias, int bias_bf16, long long stride_bias, int bias_rows, int act) {
   const int b = blockIdx.z;
   const int j = blockIdx.y;
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < m; i += gridDim.x * blockDim.x) {
@@ -185,10 +186,11 @@ __global__ void gemm_k0_kernel(void* c, long long ldc, long long stride_c, int m
         v = __fmul_rn(beta, cv);
       }
       if (bias) {
-        const long long bi = (long long)b * stride_bias + j;
+        const long long bi = (long long)b * stride_bias + (bias_rows ? i : j);
         v = __fadd_rn(v, bias_bf16 ? __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[bi])
                                    : static_cast<const float*>(bias)[bi]);
       }
+      v = apply_act(v, act);
       if constexpr (OUT == 0) static_cast<float*>(c)[idx] = v;
       else if constexpr (OUT == 1) static_cast<__nv_bfloat16*>(c)[idx] = __float2bfloat16_rn(v);
       else static_cast<__half*>(c)[idx] = __float2half_rn(v);
@@ -198,14 +200,14 @@ __global__ void gemm_k0_kernel(void* c, long long ldc, long long stride_c, int m
 
 cudaError_t launch_gemm_k0(int out, void* c, long long ldc, long long stride_c, int m, int n, int batch,
                            float beta, int ibeta, const void* bias, int bias_bf16, long long stride_bias,
-                           cudaStream_t s) {
+                           int bias_rows, int act, cudaStream_t s) {
   if (n > 65535 || batch > 65535) return cudaErrorInvalidValue;
   dim3 grid((m + 255) / 256, n, batch);
   switch (out) {
-    case 0: gemm_k0_kernel<0><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias); break;
-    case 1: gemm_k0_kernel<1><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias); break;
-    case 2: gemm_k0_kernel<2><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias); break;
-    case 3: gemm_k0_kernel<3><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias); break;
+    case 0: gemm_k0_kernel<0><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias, bias_rows, act); break;
+    case 1: gemm_k0_kernel<1><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias, bias_rows, act); break;
+    case 2: gemm_k0_kernel<2><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias, bias_rows, act); break;
+    case 3: gemm_k0_kernel<3><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias, bias_rows, act); break;
     default: return cudaErrorInvalidValue;
   }
   return cudaGetLastError();

@@ -151,6 +151,33 @@ grxdnnStatus_t grxdnnLayerNormForward(grxdnnHandle_t handle, int rows, int hidde
                                          rstd, ctx.stream));
 }
 
+grxdnnStatus_t grxdnnSoftmaxForward(grxdnnHandle_t handle, int rows, int cols, const void* x, grxDataType_t xType,
+                                    long long ldx, void* y, grxDataType_t yType, long long ldy) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (rows < 0 || cols < 0) return GRXDNN_STATUS_INVALID_VALUE;
+  if (rows == 0) return GRXDNN_STATUS_SUCCESS;
+  if (cols == 0 || !x || !y || ldx < cols || ldy < cols) return GRXDNN_STATUS_INVALID_VALUE;
+  if (xType != yType || norm_dtype(xType) < 0) return GRXDNN_STATUS_NOT_SUPPORTED;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  const grxdnnStatus_t s = ensure(ctx, false);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  return from_cuda(grx::launch_softmax(rows, cols, norm_dtype(xType), x, ldx, y, ldy, ctx.stream));
+}
+
+grxdnnStatus_t grxdnnGeluForward(grxdnnHandle_t handle, long long n, const void* x, grxDataType_t xType, void* y,
+                                 grxDataType_t yType, grxdnnGeluMode_t mode) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (n < 0 || (unsigned)mode > 1u) return GRXDNN_STATUS_INVALID_VALUE;
+  if (n == 0) return GRXDNN_STATUS_SUCCESS;
+  if (!x || !y) return GRXDNN_STATUS_INVALID_VALUE;
+  if (xType != yType || norm_dtype(xType) < 0) return GRXDNN_STATUS_NOT_SUPPORTED;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  const grxdnnStatus_t s = ensure(ctx, false);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  const int act = mode == GRXDNN_GELU_ERF ? 3 /*kActGeluErf*/ : 2 /*kActGeluTanh*/;
+  return from_cuda(grx::launch_gelu(n, norm_dtype(xType), x, y, act, ctx.dev.num_sms, ctx.stream));
+}
+
 grxdnnStatus_t grxdnnAttentionForward(grxdnnHandle_t handle, const grxdnnAttnTensor_t* qd, const void* q,
                                       const grxdnnAttnTensor_t* kd, const void* k, const grxdnnAttnTensor_t* vd,
                                       const void* v, const grxdnnAttnTensor_t* od, void* o, float scale, int causal,

@@ -132,7 +132,7 @@ extern "C" grxblasStatus_t grxblasGemmExNoAlloc(grxStream_t stream, grxblasOpera
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
 
   if (k == 0)
-    return status_of(grx::launch_gemm_k0(out, C, ldc, 0, m, n, 1, *beta, (int)*beta, nullptr, 0, 0, s));
+    return status_of(grx::launch_gemm_k0(out, C, ldc, 0, m, n, 1, *beta, (int)*beta, nullptr, 0, 0, 0, 0, s));
 
   // Operands TMA cannot read as stored are packed K-major into the static scratch.
   const bool pack_a = !grx::tma_operand_ok(A, lda, 0, es, 1);

@@ -26,6 +26,7 @@
 
 #include <mutex>
 
+#include "activation.cuh"
 #include "gemm_tc.cuh"
 #include "ptx.cuh"
 
@@ -89,10 +90,11 @@ __device__ __forceinline__ float epi_scaled(const TcGemmParams& p, uint32_t raw,
   if (p.scale_mode == 2) v = __fmul_rn(v, sb[j]);
   return v;
 }
+// + bias (over columns j, or the row's value bias_row), then the activation.
 __device__ __forceinline__ float epi_bias(const TcGemmParams& p, float v, const float* bias_f,
-                                          const __nv_bfloat16* bias_h, int j) {
-  if (p.bias) v = __fadd_rn(v, p.bias_bf16 ? __bfloat162float(bias_h[j]) : bias_f[j]);
-  return v;
+                                          const __nv_bfloat16* bias_h, int j, float bias_row) {
+  if (p.bias) v = __fadd_rn(v, p.bias_rows ? bias_row : (p.bias_bf16 ? __bfloat162float(bias_h[j]) : bias_f[j]));
+  return apply_act(v, p.act);
 }
 
 template <int KIND, int OUT>
@@ -107,6 +109,8 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_
   const float* sb = p.scale_b + bt * p.stride_sb;
   const float* bias_f = static_cast<const float*>(p.bias) + bt * p.stride_bias;
   const __nv_bfloat16* bias_h = static_cast<const __nv_bfloat16*>(p.bias) + bt * p.stride_bias;
+  const float bias_row = (p.bias && p.bias_rows && row_ok) ? (p.bias_bf16 ? __bfloat162float(bias_h[i]) : bias_f[i])
+                                                           : 0.f;
   // Pair stores need an even row index for the even lane, an even ldc / batch
   // stride and a C base aligned to two elements.
   const int i_warp0 = __shfl_sync(0xffffffffu, i, 0);
@@ -137,7 +141,7 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_
         // broadcast by shuffle (instead of 32 same-address loads per lane).
         const int jl = jbase + lane;
         const float sb_l = p.scale_mode == 2 ? sb[jl] : 1.f;
-        const float bias_l = p.bias ? (p.bias_bf16 ? __bfloat162float(bias_h[jl]) : bias_f[jl]) : 0.f;
+        const float bias_l = (p.bias && !p.bias_rows) ? (p.bias_bf16 ? __bfloat162float(bias_h[jl]) : bias_f[jl]) : 0.f;
 #pragma unroll
         for (int jj = 0; jj < 32; jj += 2) {
           const float acc_a = (KIND == kKindI8) ? (float)(int)r[jj] : __uint_as_float(r[jj]);
@@ -148,9 +152,16 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_
             b = __fmul_rn(b, __shfl_sync(0xffffffffu, sb_l, jj + 1));
           }
           if (p.bias) {
-            a = __fadd_rn(a, __shfl_sync(0xffffffffu, bias_l, jj));
-            b = __fadd_rn(b, __shfl_sync(0xffffffffu, bias_l, jj + 1));
+            if (p.bias_rows) {
+              a = __fadd_rn(a, bias_row);
+              b = __fadd_rn(b, bias_row);
+            } else {
+              a = __fadd_rn(a, __shfl_sync(0xffffffffu, bias_l, jj));
+              b = __fadd_rn(b, __shfl_sync(0xffffffffu, bias_l, jj + 1));
+            }
           }
+          a = apply_act(a, p.act);
+          b = apply_act(b, p.act);
           const float other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
           const float lo = odd ? other : a, hi = odd ? b : other;  // lower row first
           const long long off = base + (long long)(jj / 2) * step;
@@ -179,7 +190,7 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_
           } else {
             float v = epi_scaled<KIND>(p, r[jj], rowmul, sb, j);
             if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
-            store_c<OUT>(p.c, idx, epi_bias(p, v, bias_f, bias_h, j));
+            store_c<OUT>(p.c, idx, epi_bias(p, v, bias_f, bias_h, j, bias_row));
           }
         }
       }

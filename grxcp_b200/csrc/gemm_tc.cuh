@@ -11,7 +11,7 @@ namespace grx {
 // The kernel refuses to run on a version mismatch (the reference's kernel ABI
 // blocks do the same, src/libs/grxblas/hgemm_abi.h:20 and
 // src/libs/grxblas/kernels/sgemm.cpp:23-27).
-constexpr uint32_t kTcGemmAbi = 2;
+constexpr uint32_t kTcGemmAbi = 3;
 
 enum TcKind : int { kKindF16 = 0, kKindI8 = 1, kKindF8 = 2 };
 enum TcOut : int { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2, kOutS32 = 3 };
@@ -31,6 +31,8 @@ struct TcGemmParams {
   long long ldc, stride_c;
   const void* bias;
   int bias_bf16;
+  int bias_rows;                   // 1: bias indexed by row i, 0: by column j
+  int act;                         // grxblasActivation_t
   long long stride_bias;
   int scale_mode;                  // 0 none, 1 per-tensor, 2 per-row/per-column
   const float* scale_a;

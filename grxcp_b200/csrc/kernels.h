@@ -27,11 +27,11 @@ int sgemm_ctas(int m, int n);
 cudaError_t launch_pack_kmajor(const void* src, int es, int src_mn_major, long long ld, long long stride, int batch,
                                int rows, int k, void* dst, long long ldp, cudaStream_t s);
 
-// The k == 0 GEMM: C = beta*C (+ bias[j]) over the m x n window of every batch
+// The k == 0 GEMM: C = act(beta*C (+ bias[j] or bias[i])) over the m x n window of every batch
 // member; out: 0 f32, 1 bf16, 2 f16, 3 s32 (integer beta).
 cudaError_t launch_gemm_k0(int out, void* c, long long ldc, long long stride_c, int m, int n, int batch,
                            float beta, int ibeta, const void* bias, int bias_bf16, long long stride_bias,
-                           cudaStream_t s);
+                           int bias_rows, int act, cudaStream_t s);
 
 cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y, int incy, cudaStream_t s);
 cudaError_t launch_sscal(int n, float alpha, float* x, int incx, cudaStream_t s);
@@ -44,6 +44,12 @@ cudaError_t launch_rmsnorm(int rows, int hidden, int dtype, const void* x, long 
 cudaError_t launch_layernorm(int rows, int hidden, int dtype, const void* x, long long ldx, const float* gamma,
                              const float* beta, float eps, void* y, long long ldy, float* mean, float* rstd,
                              cudaStream_t s);
+
+// Softmax over each row / element-wise activation (softmax.cu); dtype as norms,
+// act a grx::kAct* value.
+cudaError_t launch_softmax(int rows, int cols, int dtype, const void* x, long long ldx, void* y, long long ldy,
+                           cudaStream_t s);
+cudaError_t launch_gelu(long long n, int dtype, const void* x, void* y, int act, int num_sms, cudaStream_t s);
 
 // Test hook: one CTA waits on an mbarrier nothing ever arrives at, through the
 // same bounded wait every kernel uses, and must come back with kErrTimeoutTest

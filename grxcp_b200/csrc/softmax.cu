@@ -1,0 +1,197 @@
+// Row softmax and element-wise GELU for sm_100a (grxDNN; the reference plans
+// "softmax, GELU" among its grxDNN primitives at docs/designs/
+// grxcp_architecture.md:594 and docs/designs/grxcp_roadmap.md:864-876, and
+// implements neither).
+//
+// Softmax is HBM-bound like the norms: one 256-thread CTA per row, the row read
+// once into registers with 16-byte loads, the max and the sum of exp(x - max)
+// reduced in fp32 (warp shuffles + one smem exchange each), the result written
+// once. Rows that defeat 16-byte vectors (address, pitch or width) take the
+// element-wise kernel, which reads the row three times from L2.
+// GELU is a grid-stride element-wise pass with 16-byte vectors where possible.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <math.h>
+
+#include "activation.cuh"
+#include "kernels.h"
+
+namespace grx {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+template <typename T> struct E;
+template <> struct E<float> {
+  static __device__ __forceinline__ float f(float v) { return v; }
+  static __device__ __forceinline__ float t(float v) { return v; }
+};
+template <> struct E<__nv_bfloat16> {
+  static __device__ __forceinline__ float f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 t(float v) { return __float2bfloat16_rn(v); }
+};
+template <> struct E<__half> {
+  static __device__ __forceinline__ float f(__half v) { return __half2float(v); }
+  static __device__ __forceinline__ __half t(float v) { return __float2half_rn(v); }
+};
+
+// CTA reduction (max or sum) with a dedicated smem slot set; all threads get it.
+template <bool MAX>
+__device__ __forceinline__ float block_reduce(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = MAX ? fmaxf(v, w) : v + w;
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < kThreads / 32 ? red[lane] : (MAX ? -INFINITY : 0.f);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float w = __shfl_xor_sync(0xffffffffu, t, o);
+    t = MAX ? fmaxf(t, w) : t + w;
+  }
+  return t;
+}
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kThreads) softmax_vec_kernel(int cols, const T* __restrict__ x, long long ldx,
+                                                              T* __restrict__ y, long long ldy) {
+  constexpr int EPV = 16 / sizeof(T);
+  __shared__ float red[64];
+  const long long row = blockIdx.x;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + row * ldx);
+  uint4* yr = reinterpret_cast<uint4*>(y + row * ldy);
+  const int nvec = cols / EPV;
+  uint4 buf[NV];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int vi = threadIdx.x + v * kThreads;
+    if (vi < nvec) {
+      buf[v] = __ldcs(xr + vi);
+      const T* e = reinterpret_cast<const T*>(&buf[v]);
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) mx = fmaxf(mx, E<T>::f(e[q]));
+    }
+  }
+  mx = block_reduce<true>(mx, red);
+  float sum = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int vi = threadIdx.x + v * kThreads;
+    if (vi < nvec) {
+      const T* e = reinterpret_cast<const T*>(&buf[v]);
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) sum += expf(E<T>::f(e[q]) - mx);
+    }
+  }
+  const float inv = 1.f / block_reduce<false>(sum, red + 32);
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int vi = threadIdx.x + v * kThreads;
+    if (vi < nvec) {
+      const T* e = reinterpret_cast<const T*>(&buf[v]);
+      uint4 o;
+      T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) oe[q] = E<T>::t(expf(E<T>::f(e[q]) - mx) * inv);
+      __stcs(yr + vi, o);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) softmax_scalar_kernel(int cols, const T* __restrict__ x, long long ldx,
+                                                                 T* __restrict__ y, long long ldy) {
+  __shared__ float red[64];
+  const T* xr = x + (long long)blockIdx.x * ldx;
+  T* yr = y + (long long)blockIdx.x * ldy;
+  float mx = -INFINITY;
+  for (int c = threadIdx.x; c < cols; c += kThreads) mx = fmaxf(mx, E<T>::f(xr[c]));
+  mx = block_reduce<true>(mx, red);
+  float sum = 0.f;
+  for (int c = threadIdx.x; c < cols; c += kThreads) sum += expf(E<T>::f(xr[c]) - mx);
+  const float inv = 1.f / block_reduce<false>(sum, red + 32);
+  for (int c = threadIdx.x; c < cols; c += kThreads) yr[c] = E<T>::t(expf(E<T>::f(xr[c]) - mx) * inv);
+}
+
+template <typename T>
+cudaError_t softmax_dispatch(int rows, int cols, const void* x, long long ldx, void* y, long long ldy,
+                             cudaStream_t s) {
+  constexpr int EPV = 16 / sizeof(T);
+  const T* xt = static_cast<const T*>(x);
+  T* yt = static_cast<T*>(y);
+  const bool aligned = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0 &&
+                       cols % EPV == 0 && (ldx * (long long)sizeof(T)) % 16 == 0 &&
+                       (ldy * (long long)sizeof(T)) % 16 == 0;
+  const int nv = (cols / EPV + kThreads - 1) / kThreads;
+  if (aligned && nv <= 8) {
+    switch (nv <= 1 ? 1 : nv <= 2 ? 2 : nv <= 4 ? 4 : 8) {
+      case 1: softmax_vec_kernel<T, 1><<<rows, kThreads, 0, s>>>(cols, xt, ldx, yt, ldy); break;
+      case 2: softmax_vec_kernel<T, 2><<<rows, kThreads, 0, s>>>(cols, xt, ldx, yt, ldy); break;
+      case 4: softmax_vec_kernel<T, 4><<<rows, kThreads, 0, s>>>(cols, xt, ldx, yt, ldy); break;
+      default: softmax_vec_kernel<T, 8><<<rows, kThreads, 0, s>>>(cols, xt, ldx, yt, ldy); break;
+    }
+  } else {
+    softmax_scalar_kernel<T><<<rows, kThreads, 0, s>>>(cols, xt, ldx, yt, ldy);
+  }
+  return cudaGetLastError();
+}
+
+template <typename T>
+__global__ void gelu_kernel(long long n, const T* __restrict__ x, T* __restrict__ y, int act, int vec) {
+  constexpr int EPV = 16 / sizeof(T);
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (vec) {
+    const long long nv = n / EPV;
+    for (long long v = t0; v < nv; v += stride) {
+      uint4 b = __ldcs(reinterpret_cast<const uint4*>(x) + v);
+      T* e = reinterpret_cast<T*>(&b);
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) e[q] = E<T>::t(apply_act(E<T>::f(e[q]), act));
+      __stcs(reinterpret_cast<uint4*>(y) + v, b);
+    }
+    for (long long i = nv * EPV + t0; i < n; i += stride) y[i] = E<T>::t(apply_act(E<T>::f(x[i]), act));
+  } else {
+    for (long long i = t0; i < n; i += stride) y[i] = E<T>::t(apply_act(E<T>::f(x[i]), act));
+  }
+}
+
+template <typename T>
+cudaError_t gelu_dispatch(long long n, const void* x, void* y, int act, int num_sms, cudaStream_t s) {
+  const bool vec = reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(y) % 16 == 0;
+  long long blocks = (n / (vec ? 16 / (long long)sizeof(T) : 1) + kThreads - 1) / kThreads;
+  const long long cap = (long long)num_sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  gelu_kernel<T><<<(unsigned)blocks, kThreads, 0, s>>>(n, static_cast<const T*>(x), static_cast<T*>(y), act,
+                                                     vec ? 1 : 0);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_softmax(int rows, int cols, int dtype, const void* x, long long ldx, void* y, long long ldy,
+                           cudaStream_t s) {
+  switch (dtype) {
+    case 0: return softmax_dispatch<float>(rows, cols, x, ldx, y, ldy, s);
+    case 1: return softmax_dispatch<__nv_bfloat16>(rows, cols, x, ldx, y, ldy, s);
+    case 2: return softmax_dispatch<__half>(rows, cols, x, ldx, y, ldy, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gelu(long long n, int dtype, const void* x, void* y, int act, int num_sms, cudaStream_t s) {
+  switch (dtype) {
+    case 0: return gelu_dispatch<float>(n, x, y, act, num_sms, s);
+    case 1: return gelu_dispatch<__nv_bfloat16>(n, x, y, act, num_sms, s);
+    case 2: return gelu_dispatch<__half>(n, x, y, act, num_sms, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace grx

@@ -89,6 +89,17 @@ class Handle:
         return lib.grxdnnLayerNormForward(self.h, rows, hidden, ptr(x), dtype_code(x), ldx, ptr(gamma), ptr(beta),
                                           eps, ptr(y), dtype_code(y), ldy, ptr(mean), ptr(rstd))
 
+    def softmax(self, x, y, rows=None, cols=None, ldx=None, ldy=None) -> int:
+        rows = x.shape[0] if rows is None else rows
+        cols = x.shape[1] if cols is None else cols
+        ldx = x.stride(0) if ldx is None else ldx
+        ldy = y.stride(0) if ldy is None else ldy
+        return lib.grxdnnSoftmaxForward(self.h, rows, cols, ptr(x), dtype_code(x), ldx, ptr(y), dtype_code(y), ldy)
+
+    def gelu(self, x, y, mode: int = 0, n=None) -> int:
+        n = x.numel() if n is None else n
+        return lib.grxdnnGeluForward(self.h, n, ptr(x), dtype_code(x), ptr(y), dtype_code(y), mode)
+
     def attention(self, q, k, v, o, scale, causal, lse=None, descs=None) -> int:
         dq, dk, dv, do = descs if descs is not None else (attn_desc(q), attn_desc(k), attn_desc(v), attn_desc(o))
         return lib.grxdnnAttentionForward(self.h, C.byref(dq), ptr(q), C.byref(dk), ptr(k), C.byref(dv), ptr(v),

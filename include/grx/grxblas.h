@@ -103,7 +103,7 @@ grxblasStatus_t grxblasGemmStridedBatchedEx(
 
 /* Additive: fused epilogue of the tensor-core GEMM.
  *
- *   D(i,j) = alpha * s(i,j) * acc(i,j) + beta * C(i,j) + bias[j]
+ *   D(i,j) = act( alpha * s(i,j) * acc(i,j) + beta * C(i,j) + bias[j or i] )
  *
  * with s(i,j) = 1 (NONE), scaleA[0]*scaleB[0] (TENSOR), or scaleA[i]*scaleB[j]
  * (ROWCOL: i over the m rows of op(A), j over the n columns of op(B)). bias,
@@ -112,15 +112,26 @@ grxblasStatus_t grxblasGemmStridedBatchedEx(
  * and apply per batch member of a strided-batched call. The epilogue is
  * copied into the handle and applies to every later GemmEx call on it until
  * replaced; NULL restores the plain alpha/beta epilogue. The int32-out int8
- * pairing accepts only the plain epilogue (its result is exact by contract). */
+ * pairing accepts only the plain epilogue (its result is exact by contract).
+ * biasOverRows = 0 indexes the bias by column j (length n), 1 by row i (length
+ * m: the per-output-feature bias of a linear layer computed as C = W^T X with
+ * row-major activations). activation is applied last (GELU per the erf
+ * definition or its tanh approximation). */
 typedef enum {
   GRXBLAS_SCALE_NONE   = 0,
   GRXBLAS_SCALE_TENSOR = 1,
   GRXBLAS_SCALE_ROWCOL = 2
 } grxblasScaleMode_t;
 
+typedef enum {
+  GRXBLAS_ACT_NONE      = 0,
+  GRXBLAS_ACT_RELU      = 1,
+  GRXBLAS_ACT_GELU_TANH = 2,
+  GRXBLAS_ACT_GELU_ERF  = 3
+} grxblasActivation_t;
+
 typedef struct {
-  const void*        bias;        /* [n] per batch member, or NULL */
+  const void*        bias;        /* [n] (or [m], see biasOverRows) per batch member, or NULL */
   grxDataType_t      biasType;    /* GRX_R_32F or GRX_R_16BF */
   long long          strideBias;
   grxblasScaleMode_t scaleMode;
@@ -128,6 +139,8 @@ typedef struct {
   const float*       scaleB;      /* [1] or [n] */
   long long          strideScaleA;
   long long          strideScaleB;
+  int                biasOverRows;
+  grxblasActivation_t activation;
 } grxblasEpilogue_t;
 
 grxblasStatus_t grxblasSetEpilogue(grxblasHandle_t handle, const grxblasEpilogue_t* epilogue);

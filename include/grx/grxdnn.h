@@ -59,6 +59,26 @@ grxdnnStatus_t grxdnnLayerNormForward(grxdnnHandle_t handle, int rows, int hidde
                                       void* y, grxDataType_t yType, long long ldy,
                                       float* mean, float* rstd);
 
+/* Softmax over the last dimension of a [rows, cols] matrix:
+ *   y[r, c] = exp(x[r, c] - max_c x[r, :]) / sum_c exp(x[r, c] - max_c x[r, :])
+ * in fp32. x/y of the same type (GRX_R_16BF, GRX_R_16F or GRX_R_32F), row
+ * pitches ldx/ldy >= cols. rows == 0 is SUCCESS. */
+grxdnnStatus_t grxdnnSoftmaxForward(grxdnnHandle_t handle, int rows, int cols,
+                                    const void* x, grxDataType_t xType, long long ldx,
+                                    void* y, grxDataType_t yType, long long ldy);
+
+/* GELU over n contiguous elements, y = x * Phi(x): GRXDNN_GELU_ERF uses the
+ * erf form of the Gaussian CDF, GRXDNN_GELU_TANH its tanh approximation.
+ * fp32 arithmetic; x and y of the same type, may alias. */
+typedef enum {
+  GRXDNN_GELU_ERF  = 0,
+  GRXDNN_GELU_TANH = 1
+} grxdnnGeluMode_t;
+
+grxdnnStatus_t grxdnnGeluForward(grxdnnHandle_t handle, long long n,
+                                 const void* x, grxDataType_t xType,
+                                 void* y, grxDataType_t yType, grxdnnGeluMode_t mode);
+
 /* A [batch, heads, seq, headDim] tensor with element strides; the headDim
  * stride is 1. */
 typedef struct {

@@ -67,6 +67,8 @@ _protos = {
     "ora_layernorm": (None, [_i, _i, _vp, _ll, _vp, _vp, _d, _vp, _vp, _vp, _i]),
     "ora_attention": (None, [_i, _i, _i, _i, _vp, _vp, _vp, _d, _i, _vp, _i, _i, _i, _vp, _vp, _i]),
     "ora_saxpy": (None, [_i, _f, _vp, _i, _vp, _i]),
+    "ora_softmax": (None, [_i, _i, _vp, _ll, _vp]),
+    "ora_gelu": (None, [_ll, _vp, _vp, _i]),
     "ora_sscal": (None, [_i, _f, _vp, _i]),
     "ora_sgemv": (None, [_i, _i, _i, _f, _vp, _i, _vp, _i, _f, _vp, _i]),
 }
@@ -236,3 +238,20 @@ def sgemv(trans, m, n, alpha, A, lda, x, incx, beta, y, incy):
     out = np.array(y, dtype=np.float32, copy=True)
     _lib.ora_sgemv(int(trans), m, n, alpha, _p(A), lda, _p(x), incx, beta, _p(out), incy)
     return out
+
+
+def softmax(x):
+    """Row softmax of a [rows, cols] float array in fp64 (definition)."""
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    y = np.empty((rows, cols), np.float64)
+    _lib.ora_softmax(rows, cols, _p(x), cols, _p(y))
+    return y
+
+
+def gelu(x, mode=0):
+    """GELU in fp64: mode 0 erf form, 1 tanh approximation."""
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty(x.shape, np.float64)
+    _lib.ora_gelu(x.size, _p(x), _p(y), mode)
+    return y

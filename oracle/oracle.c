@@ -15,6 +15,7 @@
  *   ora_saxpy / ora_sscal / ora_sgemv  tests/libs/test_grxblas_l12.cpp:79-175 (level 1/2)
  *   ora_gemm_f64      fp64 GEMM + epilogue (bias, scales, beta) for bf16/fp8/int8-scaled
  *                     GemmEx (no reference code: parity unpinned by the reference)
+ *   ora_softmax / ora_gelu  fp64 definitions (grxDNN softmax / GELU, planned only)
  *   ora_rmsnorm / ora_layernorm / ora_attention   fp64 definitions (grxDNN is planned only
  *                     in the reference: parity unpinned by the reference)
  *   conversions       bf16 / fp16 round-to-nearest-even, e4m3 RNE with saturation to +-448
@@ -23,6 +24,7 @@
  * expressions round exactly as written (the reference's gates are compiled the
  * same way for x86-64).
  */
+#define _GNU_SOURCE
 #include <math.h>
 #include <pthread.h>
 #include <stdint.h>
@@ -468,5 +470,27 @@ void ora_sgemv(int trans, int m, int n, float alpha, const float* A, int lda, co
       const float t1 = alpha * acc, t2 = beta * y[yi];
       y[yi] = t1 + t2;
     }
+  }
+}
+
+/* ------------------------------------------------------------ softmax / GELU */
+
+/* Row softmax in fp64 with the max-subtraction identity (definition). */
+void ora_softmax(int rows, int cols, const float* x, long long ldx, double* y) {
+  for (int r = 0; r < rows; ++r) {
+    const float* xr = x + (long long)r * ldx;
+    double mx = -INFINITY, s = 0.0;
+    for (int c = 0; c < cols; ++c) mx = xr[c] > mx ? xr[c] : mx;
+    for (int c = 0; c < cols; ++c) s += exp((double)xr[c] - mx);
+    for (int c = 0; c < cols; ++c) y[(long long)r * cols + c] = exp((double)xr[c] - mx) / s;
+  }
+}
+
+/* GELU in fp64: mode 0 x*Phi(x) via erf, mode 1 the tanh approximation. */
+void ora_gelu(long long n, const float* x, double* y, int mode) {
+  for (long long i = 0; i < n; ++i) {
+    const double v = x[i];
+    y[i] = mode == 0 ? 0.5 * v * (1.0 + erf(v / sqrt(2.0)))
+                     : 0.5 * v * (1.0 + tanh(sqrt(2.0 / M_PI) * (v + 0.044715 * v * v * v)));
   }
 }

@@ -170,3 +170,52 @@ def test_attention_refusals(dnn):
     assert dnn.attention(q, q, q, q, 0.1, True, descs=(d, d, d, d)) == N.NOT_SUPPORTED  # head_dim 64
     q2 = torch.zeros(1, 1, 128, 128, dtype=torch.float16, device="cuda")
     assert dnn.attention(q2, q2, q2, q2, 0.1, True) == N.NOT_SUPPORTED  # fp16
+
+
+# ------------------------------------------------------------------ softmax / GELU
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("rows,cols", [(64, 4096), (33, 1000), (5, 32768), (300, 7)])
+def test_softmax(dnn, dtype, rows, cols):
+    g = torch.Generator(device="cuda").manual_seed(rows + cols)
+    x = (torch.randn(rows, cols, device="cuda", generator=g) * 3).to(dtype)
+    y = torch.full_like(x, float("nan"))
+    assert dnn.softmax(x, y) == N.SUCCESS
+    torch.cuda.synchronize()
+    ref = oracle.softmax(x.float().cpu().numpy())
+    tol = (1e-5, 1e-4) if dtype == torch.float32 else (TOL_ABS, TOL_REL)
+    ok, nbad = close(y.float().cpu().numpy(), ref, *tol)
+    assert ok, nbad
+    assert np.allclose(y.float().sum(1).cpu().numpy(), 1.0, atol=5e-3 if dtype != torch.float32 else 1e-5)
+
+
+def test_softmax_strided_and_refusals(dnn):
+    base = torch.randn(10, 517, device="cuda").to(torch.bfloat16)
+    x = base[:, 1:501]
+    y = torch.zeros(10, 512, device="cuda", dtype=torch.bfloat16)
+    assert dnn.softmax(x, y[:, :500], ldx=517, ldy=512) == N.SUCCESS
+    torch.cuda.synchronize()
+    ok, nbad = close(y[:, :500].float().cpu().numpy(), oracle.softmax(x.float().cpu().numpy()))
+    assert ok, nbad
+    assert torch.all(y[:, 500:] == 0)
+    z = torch.zeros(4, 8, device="cuda", dtype=torch.int8)
+    assert dnn.softmax(z, z) == N.NOT_SUPPORTED
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("n", [1 << 20, 12345])
+def test_gelu(dnn, dtype, mode, n):
+    g = torch.Generator(device="cuda").manual_seed(n + mode)
+    x = (torch.randn(n, device="cuda", generator=g) * 3).to(dtype)
+    y = torch.empty_like(x)
+    assert dnn.gelu(x, y, mode) == N.SUCCESS
+    torch.cuda.synchronize()
+    ref = oracle.gelu(x.float().cpu().numpy(), mode)
+    tol = (1e-5, 1e-5) if dtype == torch.float32 else (TOL_ABS, TOL_REL)
+    ok, nbad = close(y.float().cpu().numpy(), ref, *tol)
+    assert ok, nbad
+    # in place
+    assert dnn.gelu(x, x, mode) == N.SUCCESS
+    torch.cuda.synchronize()
+    assert torch.equal(x, y)

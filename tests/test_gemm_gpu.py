@@ -393,3 +393,37 @@ def test_pair_path_fp8_batched_scaled(blas, monkeypatch):
     torch.cuda.synchronize()
     ok, nbad = close(dC.float().cpu().numpy(), want)
     assert ok, nbad
+
+
+# ------------------------------------------------------------------ epilogue: row bias and activations
+
+@pytest.mark.parametrize("act", [N.ACT_RELU, N.ACT_GELU_TANH, N.ACT_GELU_ERF])
+@pytest.mark.parametrize("rows", [False, True])
+def test_epilogue_bias_activation(blas, act, rows):
+    m, n, k = 384, 520, 256
+    A, B, _ = _bf16_problem(m, n, k, 31)
+    bias = (np.random.default_rng(2).standard_normal(m if rows else n) * 0.5).astype(np.float32)
+    lin = oracle.gemm_f64(1, 0, m, n, k, 1.0, A, k, B, k).reshape(n, m).T
+    lin = lin + (bias[:, None] if rows else bias[None, :])
+    if act == N.ACT_RELU:
+        want = np.maximum(lin, 0)
+    else:
+        want = oracle.gelu(lin.astype(np.float32), 0 if act == N.ACT_GELU_ERF else 1)
+    dC = torch.full((m * n,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    dbias = dev_f32(bias)
+    assert blas.set_epilogue(bias=dbias, bias_type=N.GRX_R_32F, bias_over_rows=rows, activation=act) == N.SUCCESS
+    assert blas.gemm_ex(1, 0, m, n, k, 1.0, dev_bits(oracle.encode("bf16", A)), N.GRX_R_16BF, k,
+                        dev_bits(oracle.encode("bf16", B)), N.GRX_R_16BF, k, 0.0, dC, N.GRX_R_16BF, m) == N.SUCCESS
+    torch.cuda.synchronize()
+    got = dC.float().cpu().numpy().reshape(n, m).T
+    ok, nbad = close(got, want)
+    assert ok, nbad
+
+
+def test_epilogue_activation_refused_for_exact_int8(blas):
+    d = torch.zeros(4096, dtype=torch.int8, device="cuda")
+    c = torch.zeros(1024, dtype=torch.int32, device="cuda")
+    assert blas.set_epilogue(activation=N.ACT_RELU) == N.SUCCESS
+    assert blas.gemm_ex(0, 0, 8, 4, 16, 1.0, d, N.GRX_R_8I, 8, d, N.GRX_R_8I, 16, 0.0, c, N.GRX_R_32I, 8) == \
+        N.NOT_SUPPORTED
+    assert blas.set_epilogue(activation=9) == N.INVALID_VALUE
