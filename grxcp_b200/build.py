@@ -34,6 +34,7 @@ SOURCES = [
     "attention.cu",
     "gemm_noalloc.cu",
     "softmax.cu",
+    "profile.cpp",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -30,6 +30,7 @@
 
 #include "attention.cuh"
 #include "ptx.cuh"
+#include "profile.h"
 
 namespace grx {
 
@@ -521,6 +522,7 @@ cudaError_t launch_attention_fwd(const AttnArgs& a, int num_sms, cudaStream_t s)
     attr = cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   });
   if (attr != cudaSuccess) return attr;
+  ProfLaunch prof("attn_fwd_kernel", dim3((unsigned)grid), dim3(kThreads), kSmem, s);
   attn_fwd_kernel<<<(unsigned)grid, kThreads, kSmem, s>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }

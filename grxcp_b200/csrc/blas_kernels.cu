@@ -6,6 +6,7 @@
 
 #include "activation.cuh"
 #include "kernels.h"
+#include "profile.h"
 #include "ptx.cuh"
 
 namespace grx {
@@ -121,6 +122,7 @@ int sgemm_ctas(int m, int n) {
 cudaError_t launch_sgemm(const SgemmArgs& a, cudaStream_t s) {
   dim3 grid((a.m + SG_BM - 1) / SG_BM, (a.n + SG_BN - 1) / SG_BN, a.batch);
   if (grid.y > 65535u || grid.z > 65535u) return cudaErrorInvalidValue;
+  ProfLaunch prof("sgemm_kernel", grid, dim3(SG_THREADS), 0, s);
   sgemm_kernel<<<grid, SG_THREADS, 0, s>>>(a);
   return cudaGetLastError();
 }
@@ -153,6 +155,7 @@ cudaError_t launch_pack_kmajor(const void* src, int es, int src_mn_major, long l
   const int threads = 256;
   long long blocks = (total + threads - 1) / threads;
   if (blocks > 148LL * 64) blocks = 148LL * 64;
+  ProfLaunch prof("pack_kmajor_kernel", dim3((unsigned)blocks), dim3(threads), 0, s);
   if (es == 2)
     pack_kmajor_kernel<uint16_t><<<(unsigned)blocks, threads, 0, s>>>(
         static_cast<const uint16_t*>(src), src_mn_major, ld, stride, rows, k, static_cast<uint16_t*>(dst), ldp,
@@ -203,6 +206,7 @@ cudaError_t launch_gemm_k0(int out, void* c, long long ldc, long long stride_c, 
                            int bias_rows, int act, cudaStream_t s) {
   if (n > 65535 || batch > 65535) return cudaErrorInvalidValue;
   dim3 grid((m + 255) / 256, n, batch);
+  ProfLaunch prof("gemm_k0_kernel", grid, dim3(256), 0, s);
   switch (out) {
     case 0: gemm_k0_kernel<0><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias, bias_rows, act); break;
     case 1: gemm_k0_kernel<1><<<grid, 256, 0, s>>>(c, ldc, stride_c, m, n, beta, ibeta, bias, bias_bf16, stride_bias, bias_rows, act); break;
@@ -269,17 +273,20 @@ static unsigned grid_for(long long n, int threads) {
 }
 
 cudaError_t launch_saxpy(int n, float alpha, const float* x, int incx, float* y, int incy, cudaStream_t s) {
+  ProfLaunch prof("saxpy_kernel", dim3(grid_for(n, 256)), dim3(256), 0, s);
   saxpy_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, alpha, x, incx, y, incy);
   return cudaGetLastError();
 }
 
 cudaError_t launch_sscal(int n, float alpha, float* x, int incx, cudaStream_t s) {
+  ProfLaunch prof("sscal_kernel", dim3(grid_for(n, 256)), dim3(256), 0, s);
   sscal_kernel<<<grid_for(n, 256), 256, 0, s>>>(n, alpha, x, incx);
   return cudaGetLastError();
 }
 
 cudaError_t launch_sgemv(int trans, int m, int n, float alpha, const float* a, int lda, const float* x, int incx,
                          float beta, float* y, int incy, cudaStream_t s) {
+  ProfLaunch prof(trans ? "sgemv_t_kernel" : "sgemv_n_kernel", dim3(trans ? (n + 3) / 4 : (m + 127) / 128), dim3(128), 0, s);
   if (!trans)
     sgemv_n_kernel<<<(m + 127) / 128, 128, 0, s>>>(m, n, alpha, a, lda, x, incx, beta, y, incy);
   else

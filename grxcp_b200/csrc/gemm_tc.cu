@@ -29,6 +29,7 @@
 #include "activation.cuh"
 #include "gemm_tc.cuh"
 #include "ptx.cuh"
+#include "profile.h"
 
 namespace grx {
 
@@ -641,6 +642,7 @@ static cudaError_t launch_impl(const CUtensorMap& ma, const CUtensorMap& mb, con
     attr_err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem);
   });
   if (attr_err != cudaSuccess) return attr_err;
+  ProfLaunch prof("tc_gemm_kernel", dim3(grid), dim3(kGemmThreads), kGemmSmem, s);
   kfn<<<grid, kGemmThreads, kGemmSmem, s>>>(ma, mb, p);
   return cudaGetLastError();
 }
@@ -655,6 +657,7 @@ static cudaError_t launch_pair_impl(const CUtensorMap& ma, const CUtensorMap& mb
     attr_err = cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem);
   });
   if (attr_err != cudaSuccess) return attr_err;
+  ProfLaunch prof("tc_gemm_pair_kernel", dim3(grid), dim3(kGemmThreads), kPairSmem, s);
   kfn<<<grid, kGemmThreads, kPairSmem, s>>>(ma, mb, p);
   return cudaGetLastError();
 }

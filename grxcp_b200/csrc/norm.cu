@@ -16,6 +16,7 @@
 #include <cuda_fp16.h>
 
 #include "kernels.h"
+#include "profile.h"
 
 namespace grx {
 
@@ -277,6 +278,8 @@ static cudaError_t dispatch(int rows, int hidden, const void* x, long long ldx, 
   const bool aligned16 = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (reinterpret_cast<uintptr_t>(y) % 16 == 0) &&
                          (reinterpret_cast<uintptr_t>(gamma) % 16 == 0) && hidden % EPV == 0 &&
                          (ldx * (long long)sizeof(T)) % 16 == 0 && (ldy * (long long)sizeof(T)) % 16 == 0;
+  ProfLaunch prof(!LN && aligned16 && nv <= 8 ? "norm_vec_kernel" : (aligned && nu <= 16 ? "norm_unit_kernel" : "norm_scalar_kernel"),
+                  dim3(rows), dim3(kNormThreads), 0, s);
   if (!LN && aligned16 && nv <= 8) {
 #define GRX_RMS_CASE(NVV)                                                                               \
   case NVV:                                                                                             \

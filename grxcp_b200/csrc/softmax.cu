@@ -15,6 +15,7 @@
 
 #include "activation.cuh"
 #include "kernels.h"
+#include "profile.h"
 
 namespace grx {
 
@@ -128,6 +129,7 @@ cudaError_t softmax_dispatch(int rows, int cols, const void* x, long long ldx, v
                        cols % EPV == 0 && (ldx * (long long)sizeof(T)) % 16 == 0 &&
                        (ldy * (long long)sizeof(T)) % 16 == 0;
   const int nv = (cols / EPV + kThreads - 1) / kThreads;
+  ProfLaunch prof(aligned && nv <= 8 ? "softmax_vec_kernel" : "softmax_scalar_kernel", dim3(rows), dim3(kThreads), 0, s);
   if (aligned && nv <= 8) {
     switch (nv <= 1 ? 1 : nv <= 2 ? 2 : nv <= 4 ? 4 : 8) {
       case 1: softmax_vec_kernel<T, 1><<<rows, kThreads, 0, s>>>(cols, xt, ldx, yt, ldy); break;
@@ -168,6 +170,7 @@ cudaError_t gelu_dispatch(long long n, const void* x, void* y, int act, int num_
   const long long cap = (long long)num_sms * 8;
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
+  ProfLaunch prof("gelu_kernel", dim3((unsigned)blocks), dim3(kThreads), 0, s);
   gelu_kernel<T><<<(unsigned)blocks, kThreads, 0, s>>>(n, static_cast<const T*>(x), static_cast<T*>(y), act,
                                                      vec ? 1 : 0);
   return cudaGetLastError();
