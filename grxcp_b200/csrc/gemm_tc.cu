@@ -8,16 +8,21 @@
 // C (:354-357), the int8 epilogue in exact int32 arithmetic (:352-357), and
 // masked edge tiles that never touch ld padding (:339-361).
 //
-// CTA organisation (192 threads, one CTA per SM, grid = min(tiles, SMs)):
+// CTA organisation (320 threads, one CTA per SM, grid = min(tiles, SMs)):
 //   warp 0      TMA producer: one thread streams A and B k-blocks into a
 //               kStages-deep ring of 128-byte-swizzled smem stages.
 //   warp 1      MMA issuer: one thread issues 4 tcgen05.mma per stage into a
 //               128 x 256 fp32/int32 accumulator in TMEM and commits the stage
 //               back to the producer; two accumulators (512 TMEM columns) let
 //               the epilogue of tile i overlap the main loop of tile i+1.
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time (thread = output
-//               row, so a warp's stores down a column of C are contiguous),
-//               apply alpha / scales / beta*C / bias, convert, store.
+//   warps 2..9  epilogue, two warps per TMEM lane quadrant (warp w reads lanes
+//               32*(w%4).., columns of half (w-2)/4): tcgen05.ld 32 columns at
+//               a time (thread = output row, so a warp's stores down a column
+//               of C are contiguous), apply alpha / scales / beta*C / bias /
+//               activation, convert, store. With one warp per SM
+//               sub-partition the epilogue was latency-bound (about 9 cycles
+//               per instruction, 16-20 us per tile); two per sub-partition
+//               plus the pipelined TMEM reads cut that several-fold.
 // Every mbarrier wait is bounded (ptx.cuh); a timeout aborts the CTA cleanly.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -74,15 +79,18 @@ __device__ __forceinline__ void store_c(void* c, long long idx, float v) {
 }
 
 // Epilogue of one output tile for the calling warp: 32 rows (thread = row i)
-// x kTileN columns from col0, read 32 columns at a time from TMEM at t_row.
+// x the 128 columns [cb, cb + 128) of the tile starting at column col0, read
+// from TMEM at t_row 32 columns at a time. The next chunk's tcgen05.ld is in
+// flight while the current chunk is converted and stored, and the per-column
+// scale and bias of every chunk are loaded once up front.
 //
 // Fast path (a full 32 x 32 chunk, beta == 0, C and ldc allow 2-element
 // stores): lanes 2r and 2r+1 swap one value with shfl.xor 1, so each lane
 // holds two consecutive ROWS of one column -- adjacent in column-major C --
 // and writes them with one 4-byte (16-bit C) or 8-byte (32-bit C) store; the
-// column pointer advances by ldc, with no per-element index arithmetic or
-// bounds test. Everything else (ragged edges, beta != 0) takes the
-// element-wise path, which also defines the arithmetic both paths share.
+// scale / bias / activation choices are made once per chunk, not per
+// element. Everything else (ragged edges, beta != 0) takes the element-wise
+// path, which also defines the arithmetic both paths share.
 // alpha * s(i,j) * acc, then (caller) + beta * C, then + bias[j].
 template <int KIND>
 __device__ __forceinline__ float epi_scaled(const TcGemmParams& p, uint32_t raw, float rowmul, const float* sb, int j) {
@@ -98,103 +106,147 @@ __device__ __forceinline__ float epi_bias(const TcGemmParams& p, float v, const 
   return apply_act(v, p.act);
 }
 
+template <int ACT>
+__device__ __forceinline__ void act_chunk(float (&v)[32]) {
+#pragma unroll
+  for (int jj = 0; jj < 32; ++jj) v[jj] = apply_act(v[jj], ACT);
+}
+
+// Row-invariant state of one thread's row of the tile.
+struct EpiRow {
+  long long cbase;   // element index of (row i, column 0) of this batch member's C
+  float rowmul;      // alpha times the row's scale
+  float bias_row;
+  bool row_ok, pair_ok;
+};
+
 template <int KIND, int OUT>
-__device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_row, int bt, int i, int col0) {
+__device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& er, uint32_t (&r)[32], int jbase,
+                                          float sb_l, float bias_l, const float* sb, const float* bias_f,
+                                          const __nv_bfloat16* bias_h) {
+  const int lane = threadIdx.x & 31;
+  if (er.pair_ok && jbase + 32 <= p.n) {
+    const bool odd = lane & 1;
+    // even lane: rows (i, i+1) of columns jbase+jj; odd lane: rows (i-1, i) of jbase+jj+1
+    const long long base = er.cbase - (odd ? 1 : 0) + (long long)(jbase + (odd ? 1 : 0)) * p.ldc;
+    const long long step = 2 * p.ldc;
+    if constexpr (OUT == kOutS32) {
+      int* cp = static_cast<int*>(p.c) + base;
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 2) {
+        const int a = p.ialpha * (int)r[jj], b = p.ialpha * (int)r[jj + 1];
+        const int other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
+        *reinterpret_cast<int2*>(cp) = odd ? make_int2(other, b) : make_int2(a, other);
+        cp += step;
+      }
+    } else {
+      float v[32];
+#pragma unroll
+      for (int jj = 0; jj < 32; ++jj)
+        v[jj] = __fmul_rn(er.rowmul, (KIND == kKindI8) ? (float)(int)r[jj] : __uint_as_float(r[jj]));
+      if (p.scale_mode == 2) {
+#pragma unroll
+        for (int jj = 0; jj < 32; ++jj) v[jj] = __fmul_rn(v[jj], __shfl_sync(0xffffffffu, sb_l, jj));
+      }
+      if (p.bias) {
+        if (p.bias_rows) {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) v[jj] = __fadd_rn(v[jj], er.bias_row);
+        } else {
+#pragma unroll
+          for (int jj = 0; jj < 32; ++jj) v[jj] = __fadd_rn(v[jj], __shfl_sync(0xffffffffu, bias_l, jj));
+        }
+      }
+      switch (p.act) {
+        case kActRelu: act_chunk<kActRelu>(v); break;
+        case kActGeluTanh: act_chunk<kActGeluTanh>(v); break;
+        case kActGeluErf: act_chunk<kActGeluErf>(v); break;
+        default: break;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 32; jj += 2) {
+        const float a = v[jj], b = v[jj + 1];
+        const float other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
+        const float lo = odd ? other : a, hi = odd ? b : other;  // lower row first
+        const long long off = base + (long long)(jj / 2) * step;
+        if constexpr (OUT == kOutF32) {
+          *reinterpret_cast<float2*>(static_cast<float*>(p.c) + off) = make_float2(lo, hi);
+        } else if constexpr (OUT == kOutBF16) {
+          *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.c) + off) = __floats2bfloat162_rn(lo, hi);
+        } else {
+          *reinterpret_cast<__half2*>(static_cast<__half*>(p.c) + off) = __floats2half2_rn(lo, hi);
+        }
+      }
+    }
+    return;
+  }
+  if (!er.row_ok) return;
+#pragma unroll
+  for (int jj = 0; jj < 32; ++jj) {
+    const int j = jbase + jj;
+    if (j < p.n) {
+      const long long idx = er.cbase + (long long)j * p.ldc;
+      if constexpr (OUT == kOutS32) {
+        int v = p.ialpha * (int)r[jj];
+        if (p.beta_nonzero) v += p.ibeta * static_cast<const int*>(p.c)[idx];
+        static_cast<int*>(p.c)[idx] = v;
+      } else {
+        float v = epi_scaled<KIND>(p, r[jj], er.rowmul, sb, j);
+        if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
+        store_c<OUT>(p.c, idx, epi_bias(p, v, bias_f, bias_h, j, er.bias_row));
+      }
+    }
+  }
+}
+
+constexpr int kEpiChunks = kTileN / 2 / 32;  // chunks of one epilogue warp's column half
+
+template <int KIND, int OUT>
+__device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_row, int bt, int i, int col0, int cb) {
   constexpr int kOutBytes = (OUT == kOutBF16 || OUT == kOutF16) ? 2 : 4;
   const int lane = threadIdx.x & 31;
-  const bool row_ok = i < p.m;
-  const long long cbase = (long long)bt * p.stride_c + i;
-  float rowmul = p.alpha;
-  if (p.scale_mode == 1) rowmul *= p.scale_a[bt * p.stride_sa] * p.scale_b[bt * p.stride_sb];
-  if (p.scale_mode == 2 && row_ok) rowmul *= p.scale_a[bt * p.stride_sa + i];
+  int cols = p.n - col0 - cb;
+  if (cols > kEpiChunks * 32) cols = kEpiChunks * 32;
+  const int nch = (cols + 31) / 32;
+  if (nch <= 0) return;  // warp-uniform
+  EpiRow er;
+  er.row_ok = i < p.m;
+  er.cbase = (long long)bt * p.stride_c + i;
+  er.rowmul = p.alpha;
+  if (p.scale_mode == 1) er.rowmul *= p.scale_a[bt * p.stride_sa] * p.scale_b[bt * p.stride_sb];
+  if (p.scale_mode == 2 && er.row_ok) er.rowmul *= p.scale_a[bt * p.stride_sa + i];
   const float* sb = p.scale_b + bt * p.stride_sb;
   const float* bias_f = static_cast<const float*>(p.bias) + bt * p.stride_bias;
   const __nv_bfloat16* bias_h = static_cast<const __nv_bfloat16*>(p.bias) + bt * p.stride_bias;
-  const float bias_row = (p.bias && p.bias_rows && row_ok) ? (p.bias_bf16 ? __bfloat162float(bias_h[i]) : bias_f[i])
-                                                           : 0.f;
+  er.bias_row = (p.bias && p.bias_rows && er.row_ok) ? (p.bias_bf16 ? __bfloat162float(bias_h[i]) : bias_f[i]) : 0.f;
   // Pair stores need an even row index for the even lane, an even ldc / batch
   // stride and a C base aligned to two elements.
   const int i_warp0 = __shfl_sync(0xffffffffu, i, 0);
-  const bool pair_ok = !p.beta_nonzero && (p.ldc % 2 == 0) && (p.stride_c % 2 == 0) && (i_warp0 % 2 == 0) &&
-                       ((reinterpret_cast<uintptr_t>(p.c) % (2 * kOutBytes)) == 0) && i_warp0 + 31 < p.m;
-  for (int c0 = 0; c0 < kTileN; c0 += 32) {
-    const int jbase = col0 + c0;
-    if (jbase >= p.n) break;  // warp-uniform
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(t_row + c0, r);
-    tmem_ld_wait();
-    if (pair_ok && jbase + 32 <= p.n) {
-      const bool odd = lane & 1;
-      // even lane: rows (i, i+1) of columns jbase+jj; odd lane: rows (i-1, i) of jbase+jj+1
-      const long long base = cbase - (odd ? 1 : 0) + (long long)(jbase + (odd ? 1 : 0)) * p.ldc;
-      const long long step = 2 * p.ldc;
-      if constexpr (OUT == kOutS32) {
-        int* cp = static_cast<int*>(p.c) + base;
+  er.pair_ok = !p.beta_nonzero && (p.ldc % 2 == 0) && (p.stride_c % 2 == 0) && (i_warp0 % 2 == 0) &&
+               ((reinterpret_cast<uintptr_t>(p.c) % (2 * kOutBytes)) == 0) && i_warp0 + 31 < p.m;
+  // This warp's column scales and biases: one value per lane per chunk,
+  // broadcast by shuffle in the fast path.
+  float sb_pre[kEpiChunks], bias_pre[kEpiChunks];
 #pragma unroll
-        for (int jj = 0; jj < 32; jj += 2) {
-          const int a = p.ialpha * (int)r[jj], b = p.ialpha * (int)r[jj + 1];
-          const int other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
-          *reinterpret_cast<int2*>(cp) = odd ? make_int2(other, b) : make_int2(a, other);
-          cp += step;
-        }
-      } else {
-        // This chunk's 32 column scales and biases: one load per lane, then
-        // broadcast by shuffle (instead of 32 same-address loads per lane).
-        const int jl = jbase + lane;
-        const float sb_l = p.scale_mode == 2 ? sb[jl] : 1.f;
-        const float bias_l = (p.bias && !p.bias_rows) ? (p.bias_bf16 ? __bfloat162float(bias_h[jl]) : bias_f[jl]) : 0.f;
+  for (int ci = 0; ci < kEpiChunks; ++ci) {
+    const int j = col0 + cb + ci * 32 + lane;
+    const bool ok = ci < nch && j < p.n;
+    sb_pre[ci] = (p.scale_mode == 2 && ok) ? sb[j] : 1.f;
+    bias_pre[ci] = (p.bias && !p.bias_rows && ok) ? (p.bias_bf16 ? __bfloat162float(bias_h[j]) : bias_f[j]) : 0.f;
+  }
+  uint32_t ra[32], rb[32];
+  tmem_ld_32x32b_x32(t_row + cb, ra);
 #pragma unroll
-        for (int jj = 0; jj < 32; jj += 2) {
-          const float acc_a = (KIND == kKindI8) ? (float)(int)r[jj] : __uint_as_float(r[jj]);
-          const float acc_b = (KIND == kKindI8) ? (float)(int)r[jj + 1] : __uint_as_float(r[jj + 1]);
-          float a = __fmul_rn(rowmul, acc_a), b = __fmul_rn(rowmul, acc_b);
-          if (p.scale_mode == 2) {
-            a = __fmul_rn(a, __shfl_sync(0xffffffffu, sb_l, jj));
-            b = __fmul_rn(b, __shfl_sync(0xffffffffu, sb_l, jj + 1));
-          }
-          if (p.bias) {
-            if (p.bias_rows) {
-              a = __fadd_rn(a, bias_row);
-              b = __fadd_rn(b, bias_row);
-            } else {
-              a = __fadd_rn(a, __shfl_sync(0xffffffffu, bias_l, jj));
-              b = __fadd_rn(b, __shfl_sync(0xffffffffu, bias_l, jj + 1));
-            }
-          }
-          a = apply_act(a, p.act);
-          b = apply_act(b, p.act);
-          const float other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
-          const float lo = odd ? other : a, hi = odd ? b : other;  // lower row first
-          const long long off = base + (long long)(jj / 2) * step;
-          if constexpr (OUT == kOutF32) {
-            *reinterpret_cast<float2*>(static_cast<float*>(p.c) + off) = make_float2(lo, hi);
-          } else if constexpr (OUT == kOutBF16) {
-            *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.c) + off) =
-                __floats2bfloat162_rn(lo, hi);
-          } else {
-            *reinterpret_cast<__half2*>(static_cast<__half*>(p.c) + off) = __floats2half2_rn(lo, hi);
-          }
-        }
-      }
-      continue;
-    }
-    if (row_ok) {
-#pragma unroll
-      for (int jj = 0; jj < 32; ++jj) {
-        const int j = jbase + jj;
-        if (j < p.n) {
-          const long long idx = cbase + (long long)j * p.ldc;
-          if constexpr (OUT == kOutS32) {
-            int v = p.ialpha * (int)r[jj];
-            if (p.beta_nonzero) v += p.ibeta * static_cast<const int*>(p.c)[idx];
-            static_cast<int*>(p.c)[idx] = v;
-          } else {
-            float v = epi_scaled<KIND>(p, r[jj], rowmul, sb, j);
-            if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
-            store_c<OUT>(p.c, idx, epi_bias(p, v, bias_f, bias_h, j, bias_row));
-          }
-        }
-      }
+  for (int ci = 0; ci < kEpiChunks; ci += 2) {
+    if (ci >= nch) break;
+    tmem_ld_wait_regs(ra);
+    if (ci + 1 < nch) tmem_ld_32x32b_x32(t_row + cb + (ci + 1) * 32, rb);
+    epi_chunk<KIND, OUT>(p, er, ra, col0 + cb + ci * 32, sb_pre[ci], bias_pre[ci], sb, bias_f, bias_h);
+    if (ci + 1 < nch) {
+      tmem_ld_wait_regs(rb);
+      if (ci + 2 < nch) tmem_ld_32x32b_x32(t_row + cb + (ci + 2) * 32, ra);
+      epi_chunk<KIND, OUT>(p, er, rb, col0 + cb + (ci + 1) * 32, sb_pre[ci + 1], bias_pre[ci + 1], sb, bias_f,
+                           bias_h);
     }
   }
 }
@@ -238,7 +290,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -350,7 +402,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int q = warp & 3;                           // TMEM lane quadrant this warp may access
+    const int cb = ((warp - 2) >> 2) * (kTileN / 2);  // its column half
     const int row = q * 32 + lane;
     int local = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
@@ -360,7 +413,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int bt, mt, nt;
       decode_tile(p, t, bt, mt, nt);
       epilogue_tile<KIND, OUT>(p, tmem_base + ((uint32_t)(q * 32) << 16) + b * kTileN, bt, mt * kTileM + row,
-                               nt * kTileN);
+                               nt * kTileN, cb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -383,7 +436,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //               (M = 256 over both CTAs' rows, N = 256 over both CTAs' B
 //               halves), and commits each stage / accumulator to the
 //               barriers of both CTAs.
-//   warps 2..5  epilogue of this CTA's 128 rows x 256 columns from its own
+//   warps 2..9  epilogue of this CTA's 128 rows x 256 columns from its own
 //               TMEM, then one arrival on the leader's accumulator-free barrier.
 // Per SM this halves the B bytes per FLOP of the single-CTA kernel, so the
 // same shared memory keeps the tensor pipe fed across longer L2 latency.
@@ -428,7 +481,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 8);  // 4 epilogue warps x 2 CTAs (used on the leader)
+      mbar_init(&tempty[b], 2 * kEpiWarps);  // epilogue warps of both CTAs (used on the leader)
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -544,6 +597,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     const int q = warp & 3;
+    const int cb = ((warp - 2) >> 2) * (kPairTileN / 2);
     const int row = q * 32 + lane;
     int local = 0;
     for (int t = pair; t < total; t += npairs, ++local) {
@@ -553,7 +607,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       int bt, mt, nt;
       decode_tile(p, t, bt, mt, nt);
       epilogue_tile<KIND, OUT>(p, tmem_base + ((uint32_t)(q * 32) << 16) + b * kPairTileN, bt,
-                               mt * kPairTileM + (int)rank * 128 + row, nt * kPairTileN);
+                               mt * kPairTileM + (int)rank * 128 + row, nt * kPairTileN, cb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {

@@ -58,7 +58,8 @@ constexpr int kTileN = 256;
 constexpr int kStages = 4;
 constexpr int kStageBytesA = kTileM * 128;   // 128 bytes of k per row
 constexpr int kStageBytesB = kTileN * 128;
-constexpr int kGemmThreads = 192;             // 6 warps: TMA, MMA, 4 x epilogue
+constexpr int kEpiWarps = 8;                      // two per TMEM lane quadrant, one per column half
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;  // warps: TMA, MMA, 8 x epilogue
 constexpr int kGemmSmem = kStages * (kStageBytesA + kStageBytesB) + 1024 /*align*/ + 256 /*barriers*/;
 
 // CTA-pair (cta_group::2) variant: a cluster of 2 CTAs computes a 256 x 256
