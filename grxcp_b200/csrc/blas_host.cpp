@@ -234,8 +234,18 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
   OperandPlan pb = plan_operand(B, tb ? 1 : 0, ldb, strideB, tc.es, batch);
   const size_t need_a = pa.pack ? pack_bytes(m, k, tc.es, pa.batch_eff) : 0;
   const size_t need_b = pb.pack ? pack_bytes(n, k, tc.es, pb.batch_eff) : 0;
+  // Workspace: [packed A][packed B][split-K partials and counters]. The
+  // split-K part is optional: without room for it the launch keeps the
+  // whole-tile schedule.
+  const size_t pack_total = (need_a + need_b + 255) & ~(size_t)255;
+  const size_t need_sk = grx::tc_gemm_splitk_bytes(tc.kind, m, n, k, batch, ctx.dev.num_sms);
+  uint8_t* sk_ws = nullptr;
+  if (need_sk) {
+    uint8_t* w = static_cast<uint8_t*>(workspace(ctx, pack_total + need_sk));
+    if (w) sk_ws = w + pack_total;
+  }
   if (need_a + need_b > 0) {
-    uint8_t* ws = static_cast<uint8_t*>(workspace(ctx, need_a + need_b));
+    uint8_t* ws = static_cast<uint8_t*>(workspace(ctx, sk_ws ? pack_total + need_sk : need_a + need_b));
     if (!ws) return GRXBLAS_STATUS_ALLOC_FAILED;
     const long long ldp = round_up(k, 16 / tc.es);
     if (pa.pack) {
@@ -265,6 +275,8 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
   L.ldb = pb.ld;
   L.stride_b = pb.batch_eff > 1 ? pb.stride : 0;
   L.b_mn_major = pb.mn_major;
+  L.sk_ws = sk_ws;
+  L.sk_ws_bytes = sk_ws ? need_sk : 0;
   grx::TcGemmParams& p = L.p;
   p.m = m;
   p.n = n;
@@ -457,13 +469,21 @@ size_t grxblasGetWorkspaceSize(grxblasHandle_t handle, grxblasOperation_t transa
   (void)Btype;
   if (m <= 0 || n <= 0 || k <= 0 || batchCount <= 0) return 0;
   const int es = (Atype == GRX_R_16F || Atype == GRX_R_16BF) ? 2 : 1;
-  // Upper bound: both operands packed, one copy per batch member. A call
-  // whose operands are 16-byte aligned needs none of it.
+  // Upper bound: both operands packed, one copy per batch member (a call
+  // whose operands are 16-byte aligned needs none of it), plus the split-K
+  // scratch when the tile count leaves a partly idle last wave on this device.
   (void)transa;
   (void)transb;
   (void)lda;
   (void)ldb;
+  const int kind = es == 2 ? grx::kKindF16 : (Atype == GRX_R_8I ? grx::kKindI8 : grx::kKindF8);
   size_t s = pack_bytes(m, k, es, batchCount) + pack_bytes(n, k, es, batchCount);
+  s = (s + 255) & ~(size_t)255;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess)
+    s += grx::tc_gemm_splitk_bytes(kind, m, n, k, batchCount, sms);
+  else
+    cudaGetLastError();
   return s;
 }
 

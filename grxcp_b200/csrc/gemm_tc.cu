@@ -51,6 +51,126 @@ __device__ __forceinline__ void decode_tile(const TcGemmParams& p, int t, int& b
   nt = w / gm;
 }
 
+// The work units of one CTA, in the order its producer, MMA issuer and
+// epilogue all walk them (units blockIdx.x, blockIdx.x + gridDim.x, ...).
+// Units [0, sk_dp_tiles) are whole tiles; unit sk_dp_tiles + v is k-range
+// v / sk_tiles (of sk_splits equal ranges) of tile sk_dp_tiles + v % sk_tiles.
+// Split-major order keeps the CTAs of one wave on the same k-range, so the A
+// and B slabs they share are read from L2 together, as in the whole-tile
+// schedule (a stream-K order, with each CTA on its own contiguous range of
+// k-iterations, put concurrent CTAs at unrelated k offsets and re-read A from
+// DRAM: 8192 x 1024 x 8192 went from 130 to 196 us). A unit is (tile,
+// k-blocks [kb0, kb1), split; split -1 = whole tile).
+struct WorkIter {
+  int u;
+  __device__ __forceinline__ WorkIter() : u(blockIdx.x) {}
+  __device__ __forceinline__ bool next(const TcGemmParams& p, int& tile, int& kb0, int& kb1, int& split) {
+    const int units = p.sk_dp_tiles + p.sk_tiles * p.sk_splits;
+    if (u >= units) return false;
+    if (u < p.sk_dp_tiles) {
+      tile = u;
+      kb0 = 0;
+      kb1 = p.k_blocks;
+      split = -1;
+    } else {
+      const int v = u - p.sk_dp_tiles;
+      split = v / p.sk_tiles;
+      tile = p.sk_dp_tiles + (v - split * p.sk_tiles);
+      kb0 = (int)((long long)split * p.k_blocks / p.sk_splits);
+      kb1 = (int)((long long)(split + 1) * p.k_blocks / p.sk_splits);
+    }
+    u += gridDim.x;
+    return true;
+  }
+};
+
+// Split-K partial slots. A slot holds one cut unit's 128 x 256 accumulator
+// tile as 32-bit words ordered [column chunk c / 32][column group (c % 32) / 4]
+// [row][c % 4]: a warp moves its 32 rows x 4 columns with one coalesced
+// 512-byte access of 16 bytes per lane.
+__device__ __forceinline__ size_t sk_slot_word(int chunk, int row) { return ((size_t)chunk * 8 * kTileM + row) * 4; }
+
+// The partial accumulators of one cut tile as this epilogue thread sees them:
+// split s left its tile in the slot at base + s * stride (words); split
+// `self` is this unit's own, still in TMEM.
+struct SkMerge {
+  int n, self, row;
+  const uint32_t* base;
+  size_t stride;
+};
+
+template <int KIND>
+__device__ __forceinline__ void sk_load(const SkMerge& mg, int s, int chunk, const uint32_t (&own)[32],
+                                        uint32_t (&dst)[32]) {
+  if (s == mg.self) {
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) dst[jj] = own[jj];
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(mg.base + s * mg.stride + sk_slot_word(chunk, mg.row));
+#pragma unroll
+  for (int g = 0; g < 8; ++g) {
+    const uint4 w = __ldcg(src + g * kTileM);
+    dst[4 * g] = w.x;
+    dst[4 * g + 1] = w.y;
+    dst[4 * g + 2] = w.z;
+    dst[4 * g + 3] = w.w;
+  }
+}
+
+// Replaces the 32 accumulators of chunk c0 by the sum over all splits, taken
+// in split order whichever CTA reduces (so the result does not depend on
+// arrival order): fp32 adds for the float kinds, int32 adds for i8.
+template <int KIND>
+__device__ __forceinline__ void sk_merge(const SkMerge& mg, int c0, uint32_t (&r)[32]) {
+  const int chunk = c0 >> 5;
+  uint32_t acc[32], v[32];
+  sk_load<KIND>(mg, 0, chunk, r, acc);
+#pragma unroll 1
+  for (int s = 1; s < mg.n; ++s) {
+    sk_load<KIND>(mg, s, chunk, r, v);
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
+      if (KIND == kKindI8) acc[jj] = (uint32_t)((int)acc[jj] + (int)v[jj]);
+      else acc[jj] = __float_as_uint(__fadd_rn(__uint_as_float(acc[jj]), __uint_as_float(v[jj])));
+    }
+  }
+#pragma unroll
+  for (int jj = 0; jj < 32; ++jj) r[jj] = acc[jj];
+}
+
+// The reducing warp's columns [cb, ce) of a cut tile: each 32-column chunk
+// of its own accumulator is read from TMEM, replaced by the sum over all
+// splits, and written back, so the ordinary epilogue then runs on the total.
+template <int KIND>
+__device__ __noinline__ void sk_reduce_into_tmem(const TcGemmParams& p, uint32_t t_row, const SkMerge& mg, int col0,
+                                                    int cb, int ce) {
+  for (int c0 = cb; c0 < ce; c0 += 32) {
+    if (col0 + c0 >= p.n) break;  // warp-uniform
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c0, r);
+    tmem_ld_wait_regs(r);
+    sk_merge<KIND>(mg, c0, r);
+    tmem_st_32x32b_x32(t_row + c0, r);
+  }
+  tmem_st_wait();
+}
+
+// This thread's row of a cut tile's accumulator, columns [cb, ce) of the tile,
+// TMEM -> its partial slot.
+__device__ __noinline__ void sk_store_partial(const TcGemmParams& p, uint32_t t_row, uint32_t* slot, int row,
+                                                 int col0, int cb, int ce) {
+  for (int c0 = cb; c0 < ce; c0 += 32) {
+    if (col0 + c0 >= p.n) break;  // warp-uniform
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c0, r);
+    tmem_ld_wait_regs(r);
+    uint4* d = reinterpret_cast<uint4*>(slot + sk_slot_word(c0 >> 5, row));
+#pragma unroll
+    for (int g = 0; g < 8; ++g) __stcg(d + g * kTileM, make_uint4(r[4 * g], r[4 * g + 1], r[4 * g + 2], r[4 * g + 3]));
+  }
+}
+
 // Waits without honouring the abort flag: used only to let in-flight copies
 // and MMAs land before the CTA releases its shared memory and TMEM.
 static __device__ __noinline__ void wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns, int* err) {
@@ -308,7 +428,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   WaitCtx wc{p.err_word, abort_flag, p.timeout_ns};
-  const int total = p.m_tiles * p.n_tiles * p.batch;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -317,11 +436,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_par = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      WorkIter it;
+      int t, kb0, kb1, split;
+      while (ok && it.next(p, t, kb0, kb1, split)) {
         int bt, mt, nt;
         decode_tile(p, t, bt, mt, nt);
         const int ba = bt * p.a_batch_step, bb = bt * p.b_batch_step;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bounded(&empty[stage], phase ^ 1u, wc, kErrTimeoutProducer)) {
             ok = false;
             break;
@@ -366,12 +487,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
-      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++local) {
+      WorkIter it;
+      int t, kb0, kb1, split;
+      for (; ok && it.next(p, t, kb0, kb1, split); ++local) {
         const int b = local & 1;
         if (!wait_bounded(&tempty[b], ((local >> 1) & 1) ^ 1u, wc, kErrTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * kTileN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bounded(&full[stage], phase, wc, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -385,7 +508,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                              : sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = p.b_mn_major ? sw128_desc(b_addr + kk * UK * 128, BK * 128, 1024)
                                              : sw128_desc(b_addr + kk * 32, 16, 1024);
-            mma_ss<KIND>(d_tmem, ad, bd, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+            mma_ss<KIND>(d_tmem, ad, bd, p.idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           mma_commit(&empty[stage]);
           if (++stage == kStages) {
@@ -406,14 +529,53 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int cb = ((warp - 2) >> 2) * (kTileN / 2);  // its column half
     const int row = q * 32 + lane;
     int local = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++local) {
+    WorkIter it;
+    int t, kb0, kb1, split;
+    for (; it.next(p, t, kb0, kb1, split); ++local) {
       const int b = local & 1;
       if (!wait_bounded(&tfull[b], (local >> 1) & 1, wc, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       int bt, mt, nt;
       decode_tile(p, t, bt, mt, nt);
-      epilogue_tile<KIND, OUT>(p, tmem_base + ((uint32_t)(q * 32) << 16) + b * kTileN, bt, mt * kTileM + row,
-                               nt * kTileN, cb);
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + b * kTileN;
+      if (split < 0) {
+        epilogue_tile<KIND, OUT>(p, t_row, bt, mt * kTileM + row, nt * kTileN, cb);
+      } else {
+        // A cut tile: publish this unit's partial, count it in, and let the
+        // last split of the tile to arrive reduce and write C. Nobody waits on
+        // another CTA, so the schedule needs no co-residency. Each warp owns
+        // its 32 rows x 128 columns end to end, with one arrival counter per
+        // (tile, epilogue warp): no barrier between warps.
+        const int r = t - p.sk_dp_tiles;
+        SkMerge mg;
+        mg.n = p.sk_splits;
+        mg.self = split;
+        mg.row = row;
+        mg.stride = (size_t)p.sk_tiles * (kTileN * kTileM);
+        mg.base = p.sk_part + (size_t)r * (kTileN * kTileM);
+        int* count = p.sk_count + (size_t)r * kEpiWarps + (warp - 2);
+        // The last split normally runs after all the others have arrived
+        // (units go split-major); it then reduces from its own TMEM without
+        // publishing. Otherwise it publishes and counts in like the rest.
+        int before = 0;
+        if (split == mg.n - 1) {
+          if (lane == 0) before = ld_acquire_gpu(count);
+          before = __shfl_sync(0xffffffffu, before, 0);
+        }
+        if (before != mg.n - 1) {
+          sk_store_partial(p, t_row, p.sk_part + (size_t)r * (kTileN * kTileM) + split * mg.stride, row,
+                           nt * kTileN, cb, cb + kTileN / 2);
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) before = atomicAdd(count, 1);
+          before = __shfl_sync(0xffffffffu, before, 0);
+        }
+        if (before == mg.n - 1) {
+          __threadfence();
+          sk_reduce_into_tmem<KIND>(p, t_row, mg, nt * kTileN, cb, cb + kTileN / 2);
+          epilogue_tile<KIND, OUT>(p, t_row, bt, mt * kTileM + row, nt * kTileN, cb);
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
@@ -732,6 +894,82 @@ static bool use_pair(int kind, const TcGemmParams& p, int num_sms) {
   return p.m >= kPairTileM && p.n >= kPairTileN && tiles >= 4LL * (num_sms / 2);
 }
 
+// Split-K plan for the last, partial wave of the single-CTA kernel. A
+// whole-tile schedule of T tiles on S SMs runs ceil(T / S) waves of K
+// k-blocks, the last with only R = T % S busy CTAs; with few waves that tail
+// is a large share of the time (an 8192 x 1024 x 8192 bf16 slice is 256 tiles
+// = 1.73 waves on 148 SMs). The plan keeps the floor(T / S) full waves whole
+// and cuts each of the R tail tiles into s k-ranges, choosing s in 2..8 to
+// minimise ceil(R s / S) * (ceil(K / s) + kSkWaveCost), the tail's length in
+// k-blocks with an allowance per wave of cut units for publishing and summing
+// the partials (about 11 us measured on B200, 24 k-blocks of a 128 x 256 x 64
+// bf16 step); each range keeps at least 4 k-blocks, the partials take at most
+// 64 MiB, and a plan must shorten the tail by at least 20 %. Measured on
+// B200 against whole tiles: 1024 x 1024 x 8192 1.44x, 512 x 1024 x 8192
+// 1.41x, 8192 x 1280 x 8192 1.10x, 8192 x 2048 x 8192 1.02x; shapes the plan
+// leaves whole (8192 x 1024 x 8192: cutting 108 tail tiles four ways saves
+// 20 k-blocks but costs three waves of overhead) run as before. GRX_GEMM_SPLITK=0 turns it off; GRX_GEMM_FORCE_SK=s cuts every tile
+// into min(s, 8, K) ranges (the tests use it at modest sizes).
+constexpr int kSkWaveCost = 24;
+
+struct SkPlan {
+  long long dp_tiles = 0, sk_tiles = 0;
+  int splits = 1;
+};
+
+static bool plan_splitk(long long tiles, int k_blocks, int num_sms, SkPlan& sp) {
+  if (const char* e = getenv("GRX_GEMM_SPLITK"))
+    if (e[0] == '0') return false;
+  if (tiles < 1 || k_blocks < 2 || num_sms < 1) return false;
+  constexpr long long kMaxUnits = (64ll << 20) / (kTileM * kTileN * 4);
+  if (const char* f = getenv("GRX_GEMM_FORCE_SK")) {
+    int sf = atoi(f);
+    if (sf > kSkMaxSeg) sf = kSkMaxSeg;
+    if (sf > k_blocks) sf = k_blocks;
+    if (sf < 2 || tiles * sf > kMaxUnits) return false;
+    sp.dp_tiles = 0;
+    sp.sk_tiles = tiles;
+    sp.splits = sf;
+    return true;
+  }
+  const long long rem = tiles % num_sms;
+  if (rem == 0) return false;
+  long long best = k_blocks;  // the whole-tile tail: one wave of K
+  int best_s = 1;
+  for (int sv = 2; sv <= kSkMaxSeg; ++sv) {
+    if (k_blocks / sv < 4 || rem * sv > kMaxUnits) break;
+    const long long cost = (rem * sv + num_sms - 1) / num_sms * ((k_blocks + sv - 1) / sv + kSkWaveCost);
+    if (cost < best) {
+      best = cost;
+      best_s = sv;
+    }
+  }
+  if (best_s == 1 || best * 10 > k_blocks * 8) return false;  // keep only plans that shorten the tail by >= 20 %
+  sp.dp_tiles = tiles - rem;
+  sp.sk_tiles = rem;
+  sp.splits = best_s;
+  return true;
+}
+
+static size_t splitk_bytes(const SkPlan& sp) {
+  const size_t parts = (size_t)sp.sk_tiles * sp.splits * kTileM * kTileN * sizeof(uint32_t);
+  const size_t counts = ((size_t)sp.sk_tiles * kEpiWarps * sizeof(int) + 255) & ~(size_t)255;
+  return parts + counts;
+}
+
+size_t tc_gemm_splitk_bytes(int kind, int m, int n, int k, int batch, int num_sms) {
+  if (m <= 0 || n <= 0 || k <= 0 || batch <= 0) return 0;
+  TcGemmParams p{};
+  p.m = m;
+  p.n = n;
+  p.batch = batch;
+  if (use_pair(kind, p, num_sms)) return 0;
+  const int bk = 128 / (kind == kKindF16 ? 2 : 1);
+  const long long tiles = (long long)((m + kTileM - 1) / kTileM) * ((n + kTileN - 1) / kTileN) * batch;
+  SkPlan sp;
+  return plan_splitk(tiles, (k + bk - 1) / bk, num_sms, sp) ? splitk_bytes(sp) : 0;
+}
+
 cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stream) {
   const int es = L.kind == kKindF16 ? 2 : 1;
   TcGemmParams p = L.p;
@@ -778,7 +1016,23 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
       default: return cudaErrorNotSupported;
     }
   }
-  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  p.sk_dp_tiles = (int)tiles;
+  p.sk_tiles = 0;
+  p.sk_splits = 1;
+  SkPlan sp;
+  if (L.sk_ws && plan_splitk(tiles, p.k_blocks, num_sms, sp) && L.sk_ws_bytes >= splitk_bytes(sp)) {
+    p.sk_dp_tiles = (int)sp.dp_tiles;
+    p.sk_tiles = (int)sp.sk_tiles;
+    p.sk_splits = sp.splits;
+    p.sk_part = static_cast<uint32_t*>(L.sk_ws);
+    p.sk_count = reinterpret_cast<int*>(static_cast<uint8_t*>(L.sk_ws) +
+                                        (size_t)sp.sk_tiles * sp.splits * kTileM * kTileN * sizeof(uint32_t));
+    const cudaError_t e = cudaMemsetAsync(p.sk_count, 0, (size_t)sp.sk_tiles * kEpiWarps * sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+    const long long units = sp.dp_tiles + sp.sk_tiles * sp.splits;
+    grid = (int)(units < num_sms ? units : num_sms);
+  }
   switch (L.kind * 4 + L.out) {
     case kKindF16 * 4 + kOutF32: return launch_impl<kKindF16, kOutF32>(ma, mb, p, grid, stream);
     case kKindF16 * 4 + kOutBF16: return launch_impl<kKindF16, kOutBF16>(ma, mb, p, grid, stream);

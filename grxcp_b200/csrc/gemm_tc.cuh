@@ -11,7 +11,7 @@ namespace grx {
 // The kernel refuses to run on a version mismatch (the reference's kernel ABI
 // blocks do the same, src/libs/grxblas/hgemm_abi.h:20 and
 // src/libs/grxblas/kernels/sgemm.cpp:23-27).
-constexpr uint32_t kTcGemmAbi = 3;
+constexpr uint32_t kTcGemmAbi = 4;
 
 enum TcKind : int { kKindF16 = 0, kKindI8 = 1, kKindF8 = 2 };
 enum TcOut : int { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2, kOutS32 = 3 };
@@ -40,6 +40,17 @@ struct TcGemmParams {
   long long stride_sa, stride_sb;
   int* err_word;
   unsigned long long timeout_ns;
+  // Tail split-K schedule. Tiles [0, sk_dp_tiles) run whole; each of the
+  // next sk_tiles tiles is cut into sk_splits equal k-ranges, run as separate
+  // units. Per epilogue warp (32 rows x 128 columns), the last unit of a cut
+  // tile to arrive on sk_count[(tile - sk_dp_tiles) * 8 + warp] sums the
+  // fp32/int32 partials of all splits (sk_part, one 128 x 256 slot per unit)
+  // in split order, then runs the epilogue. sk_tiles == 0: whole tiles only.
+  int sk_dp_tiles;
+  int sk_tiles;
+  int sk_splits;
+  uint32_t* sk_part;
+  int* sk_count;
 };
 
 struct TcGemmLaunch {
@@ -50,6 +61,10 @@ struct TcGemmLaunch {
   const void* a; long long lda, stride_a; int a_mn_major;
   const void* b; long long ldb, stride_b; int b_mn_major;
   TcGemmParams p;
+  // Device scratch for a split-K tail (tc_gemm_splitk_bytes); null or too
+  // small: the launch keeps the whole-tile schedule.
+  void* sk_ws;
+  size_t sk_ws_bytes;
 };
 
 // Tile geometry shared by host and device.
@@ -61,6 +76,8 @@ constexpr int kStageBytesB = kTileN * 128;
 constexpr int kEpiWarps = 8;                      // two per TMEM lane quadrant, one per column half
 constexpr int kGemmThreads = 64 + 32 * kEpiWarps;  // warps: TMA, MMA, 8 x epilogue
 constexpr int kGemmSmem = kStages * (kStageBytesA + kStageBytesB) + 1024 /*align*/ + 256 /*barriers*/;
+// Most k-splits of one tile (bounds the planner).
+constexpr int kSkMaxSeg = 8;
 
 // CTA-pair (cta_group::2) variant: a cluster of 2 CTAs computes a 256 x 256
 // tile; each CTA stages 128 rows of A and 128 columns of B per k-slab.
@@ -73,6 +90,10 @@ constexpr int kPairSmem = kPairStages * 2 * kPairStageBytes + 1024 + 256;
 // Enqueues the kernel (builds the TMA tensor maps). Returns cudaErrorInvalidValue
 // when an operand does not meet TMA alignment (the caller packs it first).
 cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stream);
+
+// Bytes of scratch the split-K tail of this problem wants (0: the problem
+// runs as whole tiles). The decision matches launch_tc_gemm's.
+size_t tc_gemm_splitk_bytes(int kind, int m, int n, int k, int batch, int num_sms);
 
 // True when an operand can be fed to TMA as stored.
 bool tma_operand_ok(const void* base, long long ld, long long stride, int elem_bytes, int batch);
