@@ -400,7 +400,21 @@ def run_secondary(args, peaks, dev, stream):
     nb = nbytes + 8192 * 4
     out["layernorm"] = {"value": nb / ms / 1e6, "unit": "GB/s", "ms": ms, "frac": nb / ms / 1e6 / hbm,
                         "config": "bf16 [65536, 8192], fp32 gamma/beta, eps 1e-5"}
-    del x, y
+    # norm backward on the same shape: x and dy read, dx written (saved statistics)
+    dy = torch.randn(65536, 8192, device=dev, generator=g).to(torch.bfloat16)
+    mean = torch.empty(65536, device=dev)
+    rstd = torch.empty(65536, device=dev)
+    dgamma = torch.empty(8192, device=dev)
+    dbeta = torch.empty(8192, device=dev)
+    D.check(dh.layernorm(x, gamma, beta, 1e-5, y, mean, rstd))
+    nbw = 3 * x.numel() * 2
+    ms = _time(lambda: dh.rmsnorm_backward(dy, x, gamma, 1e-5, y, rstd, dgamma), 20, stream)
+    out["rmsnorm_backward"] = {"value": nbw / ms / 1e6, "unit": "GB/s", "ms": ms, "frac": nbw / ms / 1e6 / hbm,
+                               "config": "bf16 [65536, 8192], saved rstd, dx + fp32 dgamma"}
+    ms = _time(lambda: dh.layernorm_backward(dy, x, gamma, 1e-5, y, mean, rstd, dgamma, dbeta), 20, stream)
+    out["layernorm_backward"] = {"value": nbw / ms / 1e6, "unit": "GB/s", "ms": ms, "frac": nbw / ms / 1e6 / hbm,
+                                 "config": "bf16 [65536, 8192], saved mean/rstd, dx + fp32 dgamma/dbeta"}
+    del x, y, dy
     torch.cuda.empty_cache()
 
     # config 4: causal attention B=8 H=32 S=4096 D=128

@@ -174,6 +174,8 @@ PROTOTYPES: dict[str, tuple] = {
     "grxdnnGetStream": (i32, [vp, C.POINTER(vp)]),
     "grxdnnRMSNormForward": (i32, [vp, i32, i32, vp, i32, i64, vp, f32, vp, i32, i64, vp]),
     "grxdnnLayerNormForward": (i32, [vp, i32, i32, vp, i32, i64, vp, vp, f32, vp, i32, i64, vp, vp]),
+    "grxdnnRMSNormBackward": (i32, [vp, i32, i32, vp, i32, i64, vp, i32, i64, vp, vp, f32, vp, i32, i64, vp]),
+    "grxdnnLayerNormBackward": (i32, [vp, i32, i32, vp, i32, i64, vp, i32, i64, vp, vp, vp, f32, vp, i32, i64, vp, vp]),
     "grxdnnAttentionForward": (
         i32,
         [

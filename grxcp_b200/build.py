@@ -31,6 +31,7 @@ SOURCES = [
     "gemm_tc.cu",
     "blas_kernels.cu",
     "norm.cu",
+    "norm_bwd.cu",
     "attention.cu",
     "gemm_noalloc.cu",
     "softmax.cu",

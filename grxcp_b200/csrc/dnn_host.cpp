@@ -22,6 +22,8 @@ struct grxdnnContext {
   cudaStream_t stream = nullptr;
   std::mutex mutex;
   grx::DeviceState dev;
+  void* ws = nullptr;  // grow-only, stream-ordered scratch (norm backward)
+  size_t ws_bytes = 0;
 };
 
 namespace {
@@ -74,6 +76,75 @@ grxdnnStatus_t check_norm(grxdnnHandle_t h, int rows, int hidden, const void* x,
   return GRXDNN_STATUS_SUCCESS;
 }
 
+void* workspace(grxdnnContext& ctx, size_t bytes) {
+  std::lock_guard<std::mutex> lock(ctx.mutex);
+  if (ctx.ws_bytes >= bytes) return ctx.ws;
+  if (ctx.ws) cudaFreeAsync(ctx.ws, ctx.stream);
+  ctx.ws = nullptr;
+  ctx.ws_bytes = 0;
+  void* p = nullptr;
+  if (cudaMallocAsync(&p, bytes, ctx.stream) != cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  ctx.ws = p;
+  ctx.ws_bytes = bytes;
+  return p;
+}
+
+grxdnnStatus_t norm_backward(grxdnnHandle_t handle, bool ln, int rows, int hidden, const void* dy,
+                             grxDataType_t dyType, long long lddy, const void* x, grxDataType_t xType, long long ldx,
+                             const float* gamma, const float* mean, const float* rstd, float eps, void* dx,
+                             grxDataType_t dxType, long long lddx, float* dgamma, float* dbeta) {
+  bool empty;
+  grxdnnStatus_t s = check_norm(handle, rows, hidden, x, xType, ldx, gamma, eps, dx, dxType, lddx, empty);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  if (!empty) {
+    if (!dy || lddy < hidden) return GRXDNN_STATUS_INVALID_VALUE;
+    if (ln && ((mean == nullptr) != (rstd == nullptr))) return GRXDNN_STATUS_INVALID_VALUE;
+    if (dyType != xType) return GRXDNN_STATUS_NOT_SUPPORTED;
+  }
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  if (empty) {
+    // No rows: the parameter gradients are sums over nothing.
+    if (!dgamma && !dbeta) return GRXDNN_STATUS_SUCCESS;
+    if (hidden <= 0) return hidden < 0 ? GRXDNN_STATUS_INVALID_VALUE : GRXDNN_STATUS_SUCCESS;
+    s = ensure(ctx, false);
+    if (s != GRXDNN_STATUS_SUCCESS) return s;
+    if (dgamma) {
+      const cudaError_t e = cudaMemsetAsync(dgamma, 0, (size_t)hidden * sizeof(float), ctx.stream);
+      if (e != cudaSuccess) return from_cuda(e);
+    }
+    if (ln && dbeta) return from_cuda(cudaMemsetAsync(dbeta, 0, (size_t)hidden * sizeof(float), ctx.stream));
+    return GRXDNN_STATUS_SUCCESS;
+  }
+  s = ensure(ctx, false);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  const bool need_ws = dgamma || (ln && dbeta) || !rstd;
+  void* ws = nullptr;
+  size_t ws_bytes = 0;
+  if (need_ws) {
+    ws_bytes = grx::norm_bwd_workspace_bytes(rows, hidden, ln, ctx.dev.num_sms);
+    ws = workspace(ctx, ws_bytes);
+    if (!ws) return GRXDNN_STATUS_ALLOC_FAILED;
+  }
+  grx::NormBwdArgs a{};
+  a.rows = rows;
+  a.hidden = hidden;
+  a.dtype = norm_dtype(xType);
+  a.layernorm = ln;
+  a.x = x; a.ldx = ldx;
+  a.dy = dy; a.lddy = lddy;
+  a.gamma = gamma;
+  a.mean = ln ? mean : nullptr;
+  a.rstd = rstd;
+  a.eps = eps;
+  a.dx = dx; a.lddx = lddx;
+  a.dgamma = dgamma;
+  a.dbeta = ln ? dbeta : nullptr;
+  return from_cuda(grx::launch_norm_bwd(a, ctx.dev.num_sms, ws, ws_bytes, ctx.stream));
+}
+
 bool same_shape(const grxdnnAttnTensor_t& a, const grxdnnAttnTensor_t& b) {
   return a.batch == b.batch && a.heads == b.heads && a.seq == b.seq && a.headDim == b.headDim;
 }
@@ -105,6 +176,10 @@ grxdnnStatus_t grxdnnCreate(grxdnnHandle_t* handle) {
 grxdnnStatus_t grxdnnDestroy(grxdnnHandle_t handle) {
   if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
   auto* ctx = reinterpret_cast<grxdnnContext*>(handle);
+  if (ctx->ws) {
+    cudaFreeAsync(ctx->ws, ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
+  }
   grx::release_device(ctx->dev);
   delete ctx;
   return GRXDNN_STATUS_SUCCESS;
@@ -149,6 +224,23 @@ grxdnnStatus_t grxdnnLayerNormForward(grxdnnHandle_t handle, int rows, int hidde
   if (s != GRXDNN_STATUS_SUCCESS) return s;
   return from_cuda(grx::launch_layernorm(rows, hidden, norm_dtype(xType), x, ldx, gamma, beta, eps, y, ldy, mean,
                                          rstd, ctx.stream));
+}
+
+grxdnnStatus_t grxdnnRMSNormBackward(grxdnnHandle_t handle, int rows, int hidden, const void* dy,
+                                     grxDataType_t dyType, long long lddy, const void* x, grxDataType_t xType,
+                                     long long ldx, const float* gamma, const float* rstd, float eps, void* dx,
+                                     grxDataType_t dxType, long long lddx, float* dgamma) {
+  return norm_backward(handle, false, rows, hidden, dy, dyType, lddy, x, xType, ldx, gamma, nullptr, rstd, eps, dx,
+                       dxType, lddx, dgamma, nullptr);
+}
+
+grxdnnStatus_t grxdnnLayerNormBackward(grxdnnHandle_t handle, int rows, int hidden, const void* dy,
+                                       grxDataType_t dyType, long long lddy, const void* x, grxDataType_t xType,
+                                       long long ldx, const float* gamma, const float* mean, const float* rstd,
+                                       float eps, void* dx, grxDataType_t dxType, long long lddx, float* dgamma,
+                                       float* dbeta) {
+  return norm_backward(handle, true, rows, hidden, dy, dyType, lddy, x, xType, ldx, gamma, mean, rstd, eps, dx,
+                       dxType, lddx, dgamma, dbeta);
 }
 
 grxdnnStatus_t grxdnnSoftmaxForward(grxdnnHandle_t handle, int rows, int cols, const void* x, grxDataType_t xType,
@@ -213,8 +305,6 @@ grxdnnStatus_t grxdnnAttentionForward(grxdnnHandle_t handle, const grxdnnAttnTen
   a.lse = lse;
   a.scale = scale;
   a.causal = causal ? 1 : 0;
-  a.err_word = ctx.dev.err_word;
-  a.timeout_ns = grx::wait_timeout_ns();
   return from_cuda(grx::launch_attention_fwd(a, ctx.dev.num_sms, ctx.stream));
 }
 

@@ -47,6 +47,25 @@ cudaError_t launch_layernorm(int rows, int hidden, int dtype, const void* x, lon
 
 // Softmax over each row / element-wise activation (softmax.cu); dtype as norms,
 // act a grx::kAct* value.
+// RMSNorm / LayerNorm backward (norm_bwd.cu). mean/rstd: saved statistics
+// or null (recomputed); dgamma/dbeta may be null. ws: scratch of at least
+// norm_bwd_workspace_bytes when dgamma/dbeta are wanted or stats are null.
+struct NormBwdArgs {
+  int rows, hidden, dtype;  // dtype 0 f32, 1 bf16, 2 f16
+  bool layernorm;
+  const void* x; long long ldx;
+  const void* dy; long long lddy;
+  const float* gamma;
+  const float* mean;
+  const float* rstd;
+  float eps;
+  void* dx; long long lddx;
+  float* dgamma;
+  float* dbeta;
+};
+size_t norm_bwd_workspace_bytes(int rows, int hidden, bool layernorm, int num_sms);
+cudaError_t launch_norm_bwd(const NormBwdArgs& a, int num_sms, void* ws, size_t ws_bytes, cudaStream_t s);
+
 cudaError_t launch_softmax(int rows, int cols, int dtype, const void* x, long long ldx, void* y, long long ldy,
                            cudaStream_t s);
 cudaError_t launch_gelu(long long n, int dtype, const void* x, void* y, int act, int num_sms, cudaStream_t s);

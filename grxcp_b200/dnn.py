@@ -89,6 +89,20 @@ class Handle:
         return lib.grxdnnLayerNormForward(self.h, rows, hidden, ptr(x), dtype_code(x), ldx, ptr(gamma), ptr(beta),
                                           eps, ptr(y), dtype_code(y), ldy, ptr(mean), ptr(rstd))
 
+    def rmsnorm_backward(self, dy, x, gamma, eps, dx, rstd=None, dgamma=None) -> int:
+        """grxdnnRMSNormBackward on [rows, hidden] tensors with row pitches from strides."""
+        rows, hidden = x.shape
+        return lib.grxdnnRMSNormBackward(self.h, rows, hidden, ptr(dy), dtype_code(dy), dy.stride(0), ptr(x),
+                                         dtype_code(x), x.stride(0), ptr(gamma), ptr(rstd), eps, ptr(dx),
+                                         dtype_code(dx), dx.stride(0), ptr(dgamma))
+
+    def layernorm_backward(self, dy, x, gamma, eps, dx, mean=None, rstd=None, dgamma=None, dbeta=None) -> int:
+        """grxdnnLayerNormBackward on [rows, hidden] tensors with row pitches from strides."""
+        rows, hidden = x.shape
+        return lib.grxdnnLayerNormBackward(self.h, rows, hidden, ptr(dy), dtype_code(dy), dy.stride(0), ptr(x),
+                                           dtype_code(x), x.stride(0), ptr(gamma), ptr(mean), ptr(rstd), eps,
+                                           ptr(dx), dtype_code(dx), dx.stride(0), ptr(dgamma), ptr(dbeta))
+
     def softmax(self, x, y, rows=None, cols=None, ldx=None, ldy=None) -> int:
         rows = x.shape[0] if rows is None else rows
         cols = x.shape[1] if cols is None else cols

@@ -59,6 +59,36 @@ grxdnnStatus_t grxdnnLayerNormForward(grxdnnHandle_t handle, int rows, int hidde
                                       void* y, grxDataType_t yType, long long ldy,
                                       float* mean, float* rstd);
 
+/* RMSNorm backward (no counterpart in the reference, whose grxDNN is planned
+ * only): with r = rstd of the row and H = hidden,
+ *   dx[r, c] = r gamma[c] dy[r, c] - x[r, c] r^3 (sum_c dy gamma x) / H
+ *   dgamma[c] = sum_rows dy[r, c] x[r, c] r
+ * in fp32. dy, x and dx share one type (as the forward's x/y) and have row
+ * pitches lddy/ldx/lddx >= hidden. rstd is the forward's fp32 [rows] output,
+ * or NULL to recompute it from x with eps. dgamma (fp32 [hidden]) is
+ * overwritten, summed in a fixed order (bit-reproducible); NULL skips it.
+ * rows == 0 writes dgamma = 0. Uses handle-owned scratch (grown on demand,
+ * stream-ordered) for dgamma partial sums. */
+grxdnnStatus_t grxdnnRMSNormBackward(grxdnnHandle_t handle, int rows, int hidden,
+                                     const void* dy, grxDataType_t dyType, long long lddy,
+                                     const void* x, grxDataType_t xType, long long ldx,
+                                     const float* gamma, const float* rstd, float eps,
+                                     void* dx, grxDataType_t dxType, long long lddx,
+                                     float* dgamma);
+
+/* LayerNorm backward (no counterpart in the reference): with xh = (x - mu) r,
+ *   dx = r (dy gamma - mean_c(dy gamma) - xh mean_c(dy gamma xh))
+ *   dgamma[c] = sum_rows dy xh,   dbeta[c] = sum_rows dy
+ * mean and rstd are the forward's outputs (both given, or both NULL to
+ * recompute from x with eps). dgamma / dbeta may each be NULL. Otherwise as
+ * grxdnnRMSNormBackward. */
+grxdnnStatus_t grxdnnLayerNormBackward(grxdnnHandle_t handle, int rows, int hidden,
+                                       const void* dy, grxDataType_t dyType, long long lddy,
+                                       const void* x, grxDataType_t xType, long long ldx,
+                                       const float* gamma, const float* mean, const float* rstd,
+                                       float eps, void* dx, grxDataType_t dxType, long long lddx,
+                                       float* dgamma, float* dbeta);
+
 /* Softmax over the last dimension of a [rows, cols] matrix:
  *   y[r, c] = exp(x[r, c] - max_c x[r, :]) / sum_c exp(x[r, c] - max_c x[r, :])
  * in fp32. x/y of the same type (GRX_R_16BF, GRX_R_16F or GRX_R_32F), row

@@ -64,6 +64,7 @@ _protos = {
          _ll, _i, _i, _i],
     ),
     "ora_rmsnorm": (None, [_i, _i, _vp, _ll, _vp, _d, _vp, _vp, _i]),
+    "ora_norm_bwd": (None, [_i, _i, _i, _vp, _vp, _vp, _d, _vp, _vp, _vp]),
     "ora_layernorm": (None, [_i, _i, _vp, _ll, _vp, _vp, _d, _vp, _vp, _vp, _i]),
     "ora_attention": (None, [_i, _i, _i, _i, _vp, _vp, _vp, _d, _i, _vp, _i, _i, _i, _vp, _vp, _i]),
     "ora_saxpy": (None, [_i, _f, _vp, _i, _vp, _i]),
@@ -184,6 +185,19 @@ def rmsnorm(x, gamma, eps, nthreads=None):
     rstd = np.empty(rows, np.float64)
     _lib.ora_rmsnorm(rows, hidden, _p(x), hidden, _p(gamma), eps, _p(y), _p(rstd), nthreads or nthreads_default())
     return y, rstd
+
+
+def norm_bwd(ln, x, dy, gamma, eps):
+    """fp64 RMSNorm (ln=False) / LayerNorm (ln=True) backward: (dx, dgamma, dbeta or None)."""
+    x = np.ascontiguousarray(x, np.float32)
+    dy = np.ascontiguousarray(dy, np.float32)
+    gamma = np.ascontiguousarray(gamma, np.float32)
+    rows, hidden = x.shape
+    dx = np.empty((rows, hidden), np.float64)
+    dg = np.empty(hidden, np.float64)
+    db = np.empty(hidden, np.float64) if ln else None
+    _lib.ora_norm_bwd(1 if ln else 0, rows, hidden, _p(x), _p(dy), _p(gamma), eps, _p(dx), _p(dg), _p(db))
+    return dx, dg, db
 
 
 def layernorm(x, gamma, beta, eps, nthreads=None):

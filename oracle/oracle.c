@@ -364,6 +364,45 @@ void ora_layernorm(int rows, int hidden, const float* x, long long ldx, const fl
   run_norm(p, nthreads);
 }
 
+/* Norm backward in fp64 from the definitions (the derivative of the forward
+ * above with respect to x and gamma / beta; no reference code exists).
+ * Statistics are recomputed from x in fp64. dx dense [rows, hidden];
+ * dgamma / dbeta [hidden] (dbeta only for ln; either may be NULL). */
+void ora_norm_bwd(int ln, int rows, int hidden, const float* x, const float* dy, const float* gamma, double eps,
+                  double* dx, double* dgamma, double* dbeta) {
+  if (dgamma)
+    for (int c = 0; c < hidden; ++c) dgamma[c] = 0.0;
+  if (dbeta)
+    for (int c = 0; c < hidden; ++c) dbeta[c] = 0.0;
+  for (int r = 0; r < rows; ++r) {
+    const float* xr = x + (long long)r * hidden;
+    const float* dr = dy + (long long)r * hidden;
+    double mu = 0.0, var = 0.0;
+    if (ln) {
+      for (int c = 0; c < hidden; ++c) mu += xr[c];
+      mu /= hidden;
+      for (int c = 0; c < hidden; ++c) var += ((double)xr[c] - mu) * ((double)xr[c] - mu);
+    } else {
+      for (int c = 0; c < hidden; ++c) var += (double)xr[c] * (double)xr[c];
+    }
+    var /= hidden;
+    const double rs = 1.0 / sqrt(var + eps);
+    double sa = 0.0, sb = 0.0;
+    for (int c = 0; c < hidden; ++c) {
+      const double xh = ((double)xr[c] - mu) * rs, dxh = (double)dr[c] * (double)gamma[c];
+      sa += ln ? dxh : dxh * xr[c];
+      sb += dxh * xh;
+      if (dgamma) dgamma[c] += (double)dr[c] * xh;
+      if (dbeta) dbeta[c] += dr[c];
+    }
+    for (int c = 0; c < hidden; ++c) {
+      const double xh = ((double)xr[c] - mu) * rs, dxh = (double)dr[c] * (double)gamma[c];
+      dx[(long long)r * hidden + c] =
+          ln ? rs * (dxh - sa / hidden - xh * sb / hidden) : rs * dxh - (double)xr[c] * rs * rs * rs * sa / hidden;
+    }
+  }
+}
+
 /* ------------------------------------------------------------ attention */
 
 typedef struct {

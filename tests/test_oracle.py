@@ -21,6 +21,7 @@ from pathlib import Path
 
 import numpy as np
 import pytest
+import torch
 
 import oracle
 from gates import SGEMM_BATCHED_CASES, SGEMM_CASES, HalfSampler, gemmex_cases, int8_patterns, lcg_fill
@@ -214,3 +215,26 @@ def test_attention_matches_numpy(causal):
     assert np.allclose(lse, (mx + np.log(l))[..., 0], rtol=1e-12)
     o2, l2 = oracle.attention(q, k, v, 0.25, causal, pairs=[2], q0=10, q1=20)
     assert np.allclose(o2[0], o[2, 10:20]) and np.allclose(l2[0], lse[2, 10:20])
+
+
+@pytest.mark.parametrize("ln", [False, True])
+def test_norm_backward_oracle_matches_autograd(ln):
+    """The fp64 norm-backward restatement against torch autograd in fp64
+    (an independent derivation of the same derivative)."""
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((5, 48)).astype(np.float32)
+    dy = rng.standard_normal((5, 48)).astype(np.float32)
+    g = rng.standard_normal(48).astype(np.float32)
+    dx, dg, db = oracle.norm_bwd(ln, x, dy, g, 1e-5)
+    X = torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    G = torch.tensor(g, dtype=torch.float64, requires_grad=True)
+    Bt = torch.zeros(48, dtype=torch.float64, requires_grad=True)
+    if ln:
+        y = torch.nn.functional.layer_norm(X, (48,), G, Bt, 1e-5)
+    else:
+        y = X * torch.rsqrt((X * X).mean(1, keepdim=True) + 1e-5) * G
+    y.backward(torch.tensor(dy, dtype=torch.float64))
+    assert np.allclose(dx, X.grad.numpy(), rtol=1e-12, atol=1e-12)
+    assert np.allclose(dg, G.grad.numpy(), rtol=1e-12, atol=1e-12)
+    if ln:
+        assert np.allclose(db, Bt.grad.numpy(), rtol=1e-12, atol=1e-12)
