@@ -193,6 +193,7 @@ PROTOTYPES: dict[str, tuple] = {
             vp,
         ],
     ),
+    "grxdnnAttentionBackward": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, f32, i32, vp, vp, vp, vp, vp, vp]),
     "grxdnnGetExecutionStatus": (i32, [vp]),
     "grxdnnSoftmaxForward": (i32, [vp, i32, i32, vp, i32, i64, vp, i32, i64]),
     "grxdnnGeluForward": (i32, [vp, i64, vp, i32, vp, i32, i32]),

@@ -33,6 +33,7 @@ SOURCES = [
     "norm.cu",
     "norm_bwd.cu",
     "attention.cu",
+    "attention_bwd.cu",
     "gemm_noalloc.cu",
     "softmax.cu",
     "profile.cpp",

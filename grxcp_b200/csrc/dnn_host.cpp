@@ -308,6 +308,58 @@ grxdnnStatus_t grxdnnAttentionForward(grxdnnHandle_t handle, const grxdnnAttnTen
   return from_cuda(grx::launch_attention_fwd(a, ctx.dev.num_sms, ctx.stream));
 }
 
+grxdnnStatus_t grxdnnAttentionBackward(grxdnnHandle_t handle, const grxdnnAttnTensor_t* qd, const void* q,
+                                       const grxdnnAttnTensor_t* kd, const void* k, const grxdnnAttnTensor_t* vd,
+                                       const void* v, const grxdnnAttnTensor_t* od, const void* o,
+                                       const grxdnnAttnTensor_t* dod, const void* dout, const float* lse, float scale,
+                                       int causal, const grxdnnAttnTensor_t* dqd, void* dq,
+                                       const grxdnnAttnTensor_t* dkd, void* dk, const grxdnnAttnTensor_t* dvd,
+                                       void* dv) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (!qd || !kd || !vd || !od || !dod || !dqd || !dkd || !dvd) return GRXDNN_STATUS_INVALID_VALUE;
+  const grxdnnAttnTensor_t* all[8] = {qd, kd, vd, od, dod, dqd, dkd, dvd};
+  for (auto* d : all)
+    if (d->batch < 0 || d->heads < 0 || d->seq < 0 || d->headDim <= 0 || d->strideSeq < d->headDim)
+      return GRXDNN_STATUS_INVALID_VALUE;
+  if (!same_shape(*qd, *od) || !same_shape(*qd, *dod) || !same_shape(*qd, *dqd) || !same_shape(*kd, *vd) ||
+      !same_shape(*kd, *dkd) || !same_shape(*kd, *dvd))
+    return GRXDNN_STATUS_INVALID_VALUE;
+  if (qd->batch != kd->batch || qd->headDim != kd->headDim) return GRXDNN_STATUS_INVALID_VALUE;
+  if (qd->batch == 0 || qd->heads == 0 || qd->seq == 0) return GRXDNN_STATUS_SUCCESS;
+  if (!q || !k || !v || !o || !dout || !lse || !dq || !dk || !dv) return GRXDNN_STATUS_INVALID_VALUE;
+  if (!(scale > 0.0f) || isinf(scale)) return GRXDNN_STATUS_INVALID_VALUE;
+  if (causal && qd->seq != kd->seq) return GRXDNN_STATUS_NOT_SUPPORTED;
+  if (kd->seq == 0) return GRXDNN_STATUS_NOT_SUPPORTED;
+  for (auto* d : all)
+    if (d->dtype != GRX_R_16BF) return GRXDNN_STATUS_NOT_SUPPORTED;
+  if (qd->headDim != 128 || qd->heads != kd->heads) return GRXDNN_STATUS_NOT_SUPPORTED;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  grxdnnStatus_t s = ensure(ctx, true);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  grx::AttnBwdArgs a{};
+  a.batch = qd->batch;
+  a.heads = qd->heads;
+  a.seq_q = qd->seq;
+  a.seq_k = kd->seq;
+  a.q = q; a.q_sb = qd->strideBatch; a.q_sh = qd->strideHead; a.q_ss = qd->strideSeq;
+  a.k = k; a.k_sb = kd->strideBatch; a.k_sh = kd->strideHead; a.k_ss = kd->strideSeq;
+  a.v = v; a.v_sb = vd->strideBatch; a.v_sh = vd->strideHead; a.v_ss = vd->strideSeq;
+  a.o = o; a.o_sb = od->strideBatch; a.o_sh = od->strideHead; a.o_ss = od->strideSeq;
+  a.dout = dout; a.do_sb = dod->strideBatch; a.do_sh = dod->strideHead; a.do_ss = dod->strideSeq;
+  a.lse = lse;
+  a.dq = dq; a.dq_sb = dqd->strideBatch; a.dq_sh = dqd->strideHead; a.dq_ss = dqd->strideSeq;
+  a.dk = dk; a.dk_sb = dkd->strideBatch; a.dk_sh = dkd->strideHead; a.dk_ss = dkd->strideSeq;
+  a.dv = dv; a.dv_sb = dvd->strideBatch; a.dv_sh = dvd->strideHead; a.dv_ss = dvd->strideSeq;
+  a.scale = scale;
+  a.causal = causal ? 1 : 0;
+  a.err_word = ctx.dev.err_word;
+  a.timeout_ns = grx::wait_timeout_ns();
+  const size_t need = grx::attention_bwd_workspace_bytes(a);
+  void* ws = workspace(ctx, need);
+  if (!ws) return GRXDNN_STATUS_ALLOC_FAILED;
+  return from_cuda(grx::launch_attention_bwd(a, ws, need, ctx.stream));
+}
+
 grxdnnStatus_t grxdnnGetExecutionStatus(grxdnnHandle_t handle) {
   if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
   auto* ctx = reinterpret_cast<grxdnnContext*>(handle);

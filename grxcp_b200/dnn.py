@@ -114,6 +114,14 @@ class Handle:
         n = x.numel() if n is None else n
         return lib.grxdnnGeluForward(self.h, n, ptr(x), dtype_code(x), ptr(y), dtype_code(y), mode)
 
+    def attention_backward(self, q, k, v, o, dout, lse, scale, causal, dq, dk, dv) -> int:
+        """grxdnnAttentionBackward on [B, H, S, D] tensors (descriptors from strides)."""
+        ds = [attn_desc(t) for t in (q, k, v, o, dout, dq, dk, dv)]
+        return lib.grxdnnAttentionBackward(self.h, C.byref(ds[0]), ptr(q), C.byref(ds[1]), ptr(k), C.byref(ds[2]),
+                                           ptr(v), C.byref(ds[3]), ptr(o), C.byref(ds[4]), ptr(dout), ptr(lse),
+                                           scale, 1 if causal else 0, C.byref(ds[5]), ptr(dq), C.byref(ds[6]),
+                                           ptr(dk), C.byref(ds[7]), ptr(dv))
+
     def attention(self, q, k, v, o, scale, causal, lse=None, descs=None) -> int:
         dq, dk, dv, do = descs if descs is not None else (attn_desc(q), attn_desc(k), attn_desc(v), attn_desc(o))
         return lib.grxdnnAttentionForward(self.h, C.byref(dq), ptr(q), C.byref(dk), ptr(k), C.byref(dv), ptr(v),

@@ -133,6 +133,26 @@ grxdnnStatus_t grxdnnAttentionForward(grxdnnHandle_t handle,
 
 /* Synchronises the handle's stream; EXECUTION_FAILED if a kernel launched
  * through this handle gave up on a bounded wait since the last query. */
+/* Attention backward (no counterpart in the reference): gradients of
+ * grxdnnAttentionForward. From Q, K, V, the forward's O and LSE, and dO:
+ *   P = exp(scale Q K^T - LSE) (masked as in the forward), Delta = rowsum(dO * O),
+ *   dV = P^T dO,  dS = P * (dO V^T - Delta),  dK = scale dS^T Q,  dQ = scale dS K.
+ * fp32 accumulation, bf16 outputs; every tensor bf16 with headDim 128 in its
+ * own descriptor (dq/dO/o shaped as q, dk/dv shaped as k), lse fp32
+ * [batch, heads, seq_q] as the forward wrote it. Bit-reproducible (no
+ * atomics). Uses handle-owned scratch (4 bytes per query row). Argument rules
+ * as grxdnnAttentionForward. */
+grxdnnStatus_t grxdnnAttentionBackward(grxdnnHandle_t handle,
+                                       const grxdnnAttnTensor_t* qDesc, const void* q,
+                                       const grxdnnAttnTensor_t* kDesc, const void* k,
+                                       const grxdnnAttnTensor_t* vDesc, const void* v,
+                                       const grxdnnAttnTensor_t* oDesc, const void* o,
+                                       const grxdnnAttnTensor_t* dODesc, const void* dO,
+                                       const float* lse, float scale, int causal,
+                                       const grxdnnAttnTensor_t* dQDesc, void* dQ,
+                                       const grxdnnAttnTensor_t* dKDesc, void* dK,
+                                       const grxdnnAttnTensor_t* dVDesc, void* dV);
+
 grxdnnStatus_t grxdnnGetExecutionStatus(grxdnnHandle_t handle);
 
 #ifdef __cplusplus

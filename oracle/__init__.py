@@ -67,6 +67,7 @@ _protos = {
     "ora_norm_bwd": (None, [_i, _i, _i, _vp, _vp, _vp, _d, _vp, _vp, _vp]),
     "ora_layernorm": (None, [_i, _i, _vp, _ll, _vp, _vp, _d, _vp, _vp, _vp, _i]),
     "ora_attention": (None, [_i, _i, _i, _i, _vp, _vp, _vp, _d, _i, _vp, _i, _i, _i, _vp, _vp, _i]),
+    "ora_attention_bwd": (None, [_i, _i, _i, _i, _vp, _vp, _vp, _vp, _d, _i, _vp, _vp, _vp, _i]),
     "ora_saxpy": (None, [_i, _f, _vp, _i, _vp, _i]),
     "ora_softmax": (None, [_i, _i, _vp, _ll, _vp]),
     "ora_gelu": (None, [_ll, _vp, _vp, _i]),
@@ -228,6 +229,19 @@ def attention(q, k, v, scale, causal, pairs=None, q0=0, q1=None, nthreads=None):
     _lib.ora_attention(BH, Sq, Sk, D, _p(q), _p(k), _p(v), scale, int(causal), _p(pairs), len(pairs), q0, q1, _p(o),
                        _p(lse), nthreads or nthreads_default())
     return o, lse
+
+
+def attention_bwd(q, k, v, dout, scale, causal, nthreads=None):
+    """q, dout: [BH, Sq, D]; k, v: [BH, Sk, D] float arrays. Returns fp64 (dq, dk, dv)."""
+    q, k, v, dout = (np.ascontiguousarray(t, np.float32) for t in (q, k, v, dout))
+    BH, Sq, D = q.shape
+    Sk = k.shape[1]
+    dq = np.empty((BH, Sq, D), np.float64)
+    dk = np.empty((BH, Sk, D), np.float64)
+    dv = np.empty((BH, Sk, D), np.float64)
+    _lib.ora_attention_bwd(BH, Sq, Sk, D, _p(q), _p(k), _p(v), _p(dout), scale, int(causal), _p(dq), _p(dk), _p(dv),
+                           nthreads or nthreads_default())
+    return dq, dk, dv
 
 
 # ------------------------------------------------------------ level 1 / 2

@@ -471,6 +471,94 @@ void ora_attention(int BH, int Sq, int Sk, int D, const float* q, const float* k
   free(th);
 }
 
+/* Attention backward in fp64 from the definitions (the reference has no
+ * attention): for each (b, h) pair and query row i, with P the masked softmax
+ * of scale * q_i . k_j, O_i = sum_j P_ij v_j, Delta_i = dO_i . O_i:
+ *   dV_j += P_ij dO_i,  dS_ij = P_ij (dO_i . v_j - Delta_i),
+ *   dQ_i += scale dS_ij k_j,  dK_j += scale dS_ij q_i.
+ * q, dout [BH, Sq, D]; k, v [BH, Sk, D]; outputs dense fp64 of the same
+ * shapes, threaded over (b, h). */
+typedef struct {
+  int BH, Sq, Sk, D, causal;
+  const float *q, *k, *v, *dout;
+  double scale;
+  double *dq, *dk, *dv;
+  int tid, nthreads;
+} AttnBwdJob;
+
+static void* attn_bwd_worker(void* arg) {
+  const AttnBwdJob* g = (const AttnBwdJob*)arg;
+  const int D = g->D;
+  double* pr = (double*)malloc(sizeof(double) * (size_t)g->Sk);
+  double* o = (double*)malloc(sizeof(double) * (size_t)D);
+  for (int bh = g->tid; bh < g->BH; bh += g->nthreads) {
+    const float* qb = g->q + (long long)bh * g->Sq * D;
+    const float* db = g->dout + (long long)bh * g->Sq * D;
+    const float* kb = g->k + (long long)bh * g->Sk * D;
+    const float* vb = g->v + (long long)bh * g->Sk * D;
+    double* dqb = g->dq + (long long)bh * g->Sq * D;
+    double* dkb = g->dk + (long long)bh * g->Sk * D;
+    double* dvb = g->dv + (long long)bh * g->Sk * D;
+    for (long long e = 0; e < (long long)g->Sq * D; ++e) dqb[e] = 0.0;
+    for (long long e = 0; e < (long long)g->Sk * D; ++e) dkb[e] = dvb[e] = 0.0;
+    for (int i = 0; i < g->Sq; ++i) {
+      const float* qi = qb + (long long)i * D;
+      const float* di = db + (long long)i * D;
+      const int kend = g->causal ? (i + 1 < g->Sk ? i + 1 : g->Sk) : g->Sk;
+      double mx = -INFINITY;
+      for (int j = 0; j < kend; ++j) {
+        double d = 0.0;
+        for (int c = 0; c < D; ++c) d += (double)qi[c] * (double)kb[(long long)j * D + c];
+        pr[j] = d * g->scale;
+        if (pr[j] > mx) mx = pr[j];
+      }
+      double sum = 0.0;
+      for (int j = 0; j < kend; ++j) {
+        pr[j] = exp(pr[j] - mx);
+        sum += pr[j];
+      }
+      for (int c = 0; c < D; ++c) o[c] = 0.0;
+      for (int j = 0; j < kend; ++j) {
+        pr[j] /= sum;
+        for (int c = 0; c < D; ++c) o[c] += pr[j] * (double)vb[(long long)j * D + c];
+      }
+      double delta = 0.0;
+      for (int c = 0; c < D; ++c) delta += (double)di[c] * o[c];
+      for (int j = 0; j < kend; ++j) {
+        double dp = 0.0;
+        for (int c = 0; c < D; ++c) dp += (double)di[c] * (double)vb[(long long)j * D + c];
+        const double ds = pr[j] * (dp - delta);
+        for (int c = 0; c < D; ++c) {
+          dvb[(long long)j * D + c] += pr[j] * (double)di[c];
+          dqb[(long long)i * D + c] += g->scale * ds * (double)kb[(long long)j * D + c];
+          dkb[(long long)j * D + c] += g->scale * ds * (double)qi[c];
+        }
+      }
+    }
+  }
+  free(pr);
+  free(o);
+  return 0;
+}
+
+void ora_attention_bwd(int BH, int Sq, int Sk, int D, const float* q, const float* k, const float* v,
+                       const float* dout, double scale, int causal, double* dq, double* dk, double* dv,
+                       int nthreads) {
+  if (nthreads < 1) nthreads = 1;
+  AttnBwdJob* jobs = (AttnBwdJob*)calloc((size_t)nthreads, sizeof(AttnBwdJob));
+  pthread_t* th = (pthread_t*)calloc((size_t)nthreads, sizeof(pthread_t));
+  for (int t = 0; t < nthreads; ++t) {
+    AttnBwdJob g = {BH, Sq, Sk, D, causal, q, k, v, dout, scale, dq, dk, dv, t, nthreads};
+    jobs[t] = g;
+    if (nthreads > 1) pthread_create(&th[t], 0, attn_bwd_worker, &jobs[t]);
+    else attn_bwd_worker(&jobs[t]);
+  }
+  if (nthreads > 1)
+    for (int t = 0; t < nthreads; ++t) pthread_join(th[t], 0);
+  free(jobs);
+  free(th);
+}
+
 /* ------------------------------------------------------------ level 1 / 2 */
 
 /* BLAS increment addressing (tests/libs/test_grxblas_l12.cpp:27-31). */

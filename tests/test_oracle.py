@@ -238,3 +238,21 @@ def test_norm_backward_oracle_matches_autograd(ln):
     assert np.allclose(dg, G.grad.numpy(), rtol=1e-12, atol=1e-12)
     if ln:
         assert np.allclose(db, Bt.grad.numpy(), rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("causal,sq,sk", [(True, 7, 7), (False, 5, 9)])
+def test_attention_backward_oracle_matches_autograd(causal, sq, sk):
+    """The fp64 attention-backward restatement against torch autograd in fp64."""
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((2, sq, 16)).astype(np.float32)
+    k = rng.standard_normal((2, sk, 16)).astype(np.float32)
+    v = rng.standard_normal((2, sk, 16)).astype(np.float32)
+    do = rng.standard_normal((2, sq, 16)).astype(np.float32)
+    dq, dk, dv = oracle.attention_bwd(q, k, v, do, 0.3, causal)
+    Q, K, V = (torch.tensor(t, dtype=torch.float64, requires_grad=True) for t in (q, k, v))
+    s = Q @ K.transpose(1, 2) * 0.3
+    if causal:
+        s = s.masked_fill(torch.ones(sq, sk, dtype=torch.bool).triu(1), float("-inf"))
+    (torch.softmax(s, -1) @ V).backward(torch.tensor(do, dtype=torch.float64))
+    for got, ref in ((dq, Q.grad), (dk, K.grad), (dv, V.grad)):
+        assert np.allclose(got, ref.numpy(), rtol=1e-10, atol=1e-12)
