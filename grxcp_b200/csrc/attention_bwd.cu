@@ -15,12 +15,13 @@
 //       and dO_i stay resident while it walks the key blocks; dQ_i accumulates
 //       in TMEM. It recomputes S and dP instead of sharing dS with the KV
 //       kernel through fp32 atomics.
-// CTA: 192 threads. Warp 0 is the TMA producer (one thread): the resident pair
+// CTA: 320 threads. Warp 0 is the TMA producer (one thread): the resident pair
 // once, then the streamed pair of each block through a 2-stage ring. Warp 1 is
 // the MMA issuer (one thread): per block S = Q K^T and dP = dO V^T (K-major
 // operands, 128 x 128 x 128 each), then dV += P^T dO and dK += dS^T Q (KV
-// kernel) or dQ += dS K (Q kernel). Warps 2..5 (thread = TMEM lane = query
-// row) read S and dP from TMEM 32 columns at a time, form P and dS in fp32 and
+// kernel) or dQ += dS K (Q kernel). Warps 2..9, two per TMEM lane quadrant
+// (thread = query row; warp w takes columns [64 (w-2)/4, +64)), read S and dP
+// from TMEM 32 columns at a time, form P and dS in fp32 and
 // write them as bf16 into one 128 x 128 shared-memory tile in the same
 // 128-byte-swizzled layout TMA gives a loaded tile (rows = queries). Read
 // with a K-major descriptor that tile is the A operand for dQ (M = queries);
@@ -46,7 +47,8 @@ constexpr int kD = 128;
 constexpr int kB = 128;                   // queries or keys per block
 constexpr int kTile = kB * kD * 2;        // 32 KiB bf16 tile (two 16 KiB swizzle halves)
 constexpr int kHalf = 16384;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kComputeWarps = 8;  // two per TMEM lane quadrant, one per 64-column half
 constexpr int kModeKV = 0, kModeQ = 1;
 // Resident pair (K,V or Q,dO), a 2-stage ring of streamed pairs, the P/dS tile.
 constexpr int kSmem = 2 * kTile + 2 * 2 * kTile + kTile + 1024 + 256;
@@ -175,9 +177,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&ring_empty[s], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
+    mbar_init(p_full, kComputeWarps);
     mbar_init(ps_read, 1);
-    mbar_init(ds_full, 4);
+    mbar_init(ds_full, kComputeWarps);
     mbar_init(ps_free, 1);
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
@@ -304,6 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ P / dS and the epilogue
     const int q = warp & 3;
+    const int cb = ((warp - 2) >> 2) * 64;  // this warp's 64 of the 128 key (or head-dim) columns
     const int row = q * 32 + lane;
     const uint32_t t_row = tmem + ((uint32_t)(q * 32) << 16);
     const uint32_t ps = smem_u32(sPS);
@@ -320,12 +323,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       // The P/dS tile still holds the previous block's dS until its MMA ends.
       if (t > 0 && !wait_bounded(ps_free, (t - 1) & 1, wc, kErrTimeoutEpilogue)) break;
-      uint32_t ds_pk[MODE == kModeKV ? 64 : 1];
+      uint32_t ds_pk[MODE == kModeKV ? 32 : 1];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
+        const int col = cb + c * 32;
         uint32_t rs[32], rd[32];
-        tmem_ld_32x32b_x32(t_row + c * 32, rs);
-        tmem_ld_32x32b_x32(t_row + 128 + c * 32, rd);
+        tmem_ld_32x32b_x32(t_row + col, rs);
+        tmem_ld_32x32b_x32(t_row + 128 + col, rd);
         tmem_ld_wait();
         uint32_t pp[16], dd[16];
 #pragma unroll
@@ -333,7 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float pv[2], dv[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int k = kblk * kB + c * 32 + jj + e;
+            const int k = kblk * kB + col + jj + e;
             const bool valid = qvalid && k < p.seq_k && (!p.causal || k <= qabs);
             pv[e] = valid ? ex2_approx(fmaf(__uint_as_float(rs[jj + e]), p.scale_log2, -lse_l2)) : 0.f;
             dv[e] = pv[e] * (__uint_as_float(rd[jj + e]) - dlt);
@@ -344,11 +348,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
           if (MODE == kModeKV) {
-            st_shared_v4(ps + swz_off(row, c * 32 + g * 8), pp[4 * g], pp[4 * g + 1], pp[4 * g + 2], pp[4 * g + 3]);
+            st_shared_v4(ps + swz_off(row, col + g * 8), pp[4 * g], pp[4 * g + 1], pp[4 * g + 2], pp[4 * g + 3]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) ds_pk[c * 16 + 4 * g + e] = dd[4 * g + e];
           } else {
-            st_shared_v4(ps + swz_off(row, c * 32 + g * 8), dd[4 * g], dd[4 * g + 1], dd[4 * g + 2], dd[4 * g + 3]);
+            st_shared_v4(ps + swz_off(row, col + g * 8), dd[4 * g], dd[4 * g + 1], dd[4 * g + 2], dd[4 * g + 3]);
           }
         }
       }
@@ -360,10 +364,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // dS replaces P once dV has read it.
         if (!wait_bounded(ps_read, t & 1, wc, kErrTimeoutEpilogue)) break;
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
           for (int g = 0; g < 4; ++g)
-            st_shared_v4(ps + swz_off(row, c * 32 + g * 8), ds_pk[c * 16 + 4 * g], ds_pk[c * 16 + 4 * g + 1],
+            st_shared_v4(ps + swz_off(row, cb + c * 32 + g * 8), ds_pk[c * 16 + 4 * g], ds_pk[c * 16 + 4 * g + 1],
                          ds_pk[c * 16 + 4 * g + 2], ds_pk[c * 16 + 4 * g + 3]);
         fence_async_smem();
         __syncwarp();
@@ -383,12 +387,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                              (which == 0 ? (long long)bi * p.o0_sb + (long long)hi * p.o0_sh + (long long)rabs * p.o0_ss
                                          : (long long)bi * p.o1_sb + (long long)hi * p.o1_sh + (long long)rabs * p.o1_ss);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + col + c * 32, v);
+          tmem_ld_32x32b_x32(t_row + col + cb + c * 32, v);
           tmem_ld_wait();
           if (rvalid) {
-            uint4* dst = reinterpret_cast<uint4*>(out + c * 32);
+            uint4* dst = reinterpret_cast<uint4*>(out + cb + c * 32);
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
               uint32_t w[4];
