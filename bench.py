@@ -427,7 +427,15 @@ def run_secondary(args, peaks, dev, stream):
     ms = _time(lambda: dh.attention(q, k, v, o, 1 / math.sqrt(128), True, lse), 10, stream)
     out["attention"] = {"value": fl / ms / 1e9, "unit": "TFLOP/s", "ms": ms, "frac": fl / ms / 1e9 / bf16_peak,
                         "config": "causal, bf16, B=8 H=32 S=4096 D=128, fp32 LSE; FLOP = 2*B*H*S^2*D"}
-    del q, k, v, o, lse
+    # backward of the same call (dQ, dK, dV from O, LSE and a random dO)
+    dout = torch.randn_like(q)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    ms = _time(lambda: dh.attention_backward(q, k, v, o, dout, lse, 1 / math.sqrt(128), True, dq, dk, dv), 5, stream)
+    out["attention_backward"] = {
+        "value": 2.5 * fl / ms / 1e9, "unit": "TFLOP/s", "ms": ms, "frac": 2.5 * fl / ms / 1e9 / bf16_peak,
+        "config": "causal, bf16, B=8 H=32 S=4096 D=128; FLOP = 2.5 x forward (five GEMMs); the kernels execute "
+                  "seven (S and dP are recomputed by the dQ pass instead of fp32 atomics)"}
+    del q, k, v, o, lse, dout, dq, dk, dv
     torch.cuda.empty_cache()
 
     # config 5: fp8 e4m3 strided-batched MLP GEMM, batch 16, 4096 x 14336 x 4096, per-tensor scales, bf16 out
