@@ -49,6 +49,15 @@ class grxblasEpilogue_t(C.Structure):
     ]
 
 
+class grxdnnConvDesc_t(C.Structure):
+    _fields_ = [(f, i32) for f in ("n", "h", "w", "c", "k", "r", "s", "padH", "padW", "strideH", "strideW",
+                                   "dilationH", "dilationW")]
+
+
+class grxdnnPoolDesc_t(C.Structure):
+    _fields_ = [(f, i32) for f in ("n", "h", "w", "c", "r", "s", "padH", "padW", "strideH", "strideW", "mode")]
+
+
 class grxdnnAttnTensor_t(C.Structure):
     _fields_ = [
         ("batch", i32),
@@ -193,6 +202,10 @@ PROTOTYPES: dict[str, tuple] = {
             vp,
         ],
     ),
+    "grxdnnConvOutputDims": (i32, [vp, vp, vp]),
+    "grxdnnConv2dForward": (i32, [vp, vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32]),
+    "grxdnnPoolingOutputDims": (i32, [vp, vp, vp]),
+    "grxdnnPooling2dForward": (i32, [vp, vp, vp, i32, vp, i32]),
     "grxdnnAttentionBackward": (i32, [vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, f32, i32, vp, vp, vp, vp, vp, vp]),
     "grxdnnGetExecutionStatus": (i32, [vp]),
     "grxdnnSoftmaxForward": (i32, [vp, i32, i32, vp, i32, i64, vp, i32, i64]),
@@ -223,3 +236,5 @@ STATUS = {
 SUCCESS, NOT_INITIALIZED, ALLOC_FAILED, INVALID_VALUE, ARCH_MISMATCH, EXECUTION_FAILED, NOT_SUPPORTED, INTERNAL_ERROR = range(8)
 SCALE_NONE, SCALE_TENSOR, SCALE_ROWCOL = 0, 1, 2
 ACT_NONE, ACT_RELU, ACT_GELU_TANH, ACT_GELU_ERF = 0, 1, 2, 3
+
+POOL_MAX, POOL_AVG_INCLUDE_PAD, POOL_AVG_EXCLUDE_PAD = 0, 1, 2

@@ -36,6 +36,7 @@ SOURCES = [
     "attention_bwd.cu",
     "gemm_noalloc.cu",
     "softmax.cu",
+    "conv.cu",
     "profile.cpp",
 ]
 

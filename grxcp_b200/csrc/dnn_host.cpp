@@ -14,6 +14,7 @@
 #include <mutex>
 
 #include "attention.cuh"
+#include "gemm_tc.cuh"
 #include "grx/grxdnn.h"
 #include "host_common.h"
 #include "kernels.h"
@@ -358,6 +359,109 @@ grxdnnStatus_t grxdnnAttentionBackward(grxdnnHandle_t handle, const grxdnnAttnTe
   void* ws = workspace(ctx, need);
   if (!ws) return GRXDNN_STATUS_ALLOC_FAILED;
   return from_cuda(grx::launch_attention_bwd(a, ws, need, ctx.stream));
+}
+
+grxdnnStatus_t grxdnnConvOutputDims(const grxdnnConvDesc_t* d, int* p, int* q) {
+  if (!d || !p || !q) return GRXDNN_STATUS_INVALID_VALUE;
+  if (d->h <= 0 || d->w <= 0 || d->r <= 0 || d->s <= 0 || d->padH < 0 || d->padW < 0 || d->strideH < 1 ||
+      d->strideW < 1 || d->dilationH < 1 || d->dilationW < 1)
+    return GRXDNN_STATUS_INVALID_VALUE;
+  const long long eh = (long long)d->h + 2LL * d->padH - (long long)d->dilationH * (d->r - 1) - 1;
+  const long long ew = (long long)d->w + 2LL * d->padW - (long long)d->dilationW * (d->s - 1) - 1;
+  if (eh < 0 || ew < 0) return GRXDNN_STATUS_INVALID_VALUE;
+  *p = (int)(eh / d->strideH + 1);
+  *q = (int)(ew / d->strideW + 1);
+  return GRXDNN_STATUS_SUCCESS;
+}
+
+grxdnnStatus_t grxdnnConv2dForward(grxdnnHandle_t handle, const grxdnnConvDesc_t* d, const void* x,
+                                   grxDataType_t xType, const void* w, grxDataType_t wType, const float* alpha,
+                                   const float* beta, const float* bias, int activation, void* y,
+                                   grxDataType_t yType) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (!d) return GRXDNN_STATUS_INVALID_VALUE;
+  int P = 0, Q = 0;
+  if (d->n < 0 || d->c <= 0 || d->k <= 0) return GRXDNN_STATUS_INVALID_VALUE;
+  grxdnnStatus_t s = grxdnnConvOutputDims(d, &P, &Q);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  if ((unsigned)activation > 3u) return GRXDNN_STATUS_INVALID_VALUE;
+  if (d->n == 0) return GRXDNN_STATUS_SUCCESS;
+  if (!x || !w || !y) return GRXDNN_STATUS_INVALID_VALUE;
+  const int in_dt = xType == GRX_R_16BF ? 1 : xType == GRX_R_32F ? 0 : -1;
+  const int out_dt = yType == GRX_R_16BF ? 1 : yType == GRX_R_32F ? 0 : -1;
+  if (in_dt < 0 || out_dt < 0 || wType != xType || (in_dt == 0 && out_dt != 0)) return GRXDNN_STATUS_NOT_SUPPORTED;
+  const float al = alpha ? *alpha : 1.f, be = beta ? *beta : 0.f;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  s = ensure(ctx, false);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  if (in_dt == 1 && d->c % 64 == 0 && ctx.dev.cc_major == 10) {
+    grx::TcConvLaunch L{};
+    L.out = out_dt == 1 ? grx::kOutBF16 : grx::kOutF32;
+    L.x = x;
+    L.w = w;
+    L.n = d->n; L.h = d->h; L.wd = d->w; L.c = d->c; L.k = d->k; L.r = d->r; L.s = d->s; L.p = P; L.q = Q;
+    L.pad_h = d->padH; L.pad_w = d->padW; L.stride_h = d->strideH; L.stride_w = d->strideW;
+    L.dil_h = d->dilationH; L.dil_w = d->dilationW;
+    grx::TcGemmParams& e = L.p_epi;
+    e.alpha = al;
+    e.beta = be;
+    e.beta_nonzero = be != 0.f ? 1 : 0;
+    e.c = y;
+    e.ldc = d->k;
+    e.bias = bias;
+    e.bias_rows = 1;
+    e.act = activation;
+    e.err_word = ctx.dev.err_word;
+    e.timeout_ns = grx::wait_timeout_ns();
+    e.group_m = 16;
+    const cudaError_t err = grx::launch_tc_conv(L, ctx.dev.num_sms, ctx.stream);
+    if (err != cudaErrorNotSupported) return from_cuda(err);
+    cudaGetLastError();  // not expressible as TMA boxes: the direct kernel takes it
+  }
+  grx::ConvArgs a{};
+  a.n = d->n; a.h = d->h; a.w = d->w; a.c = d->c; a.k = d->k; a.r = d->r; a.s = d->s; a.p = P; a.q = Q;
+  a.pad_h = d->padH; a.pad_w = d->padW; a.stride_h = d->strideH; a.stride_w = d->strideW;
+  a.dil_h = d->dilationH; a.dil_w = d->dilationW;
+  a.in_dtype = in_dt;
+  a.out_dtype = out_dt;
+  a.x = x; a.filt = w; a.y = y;
+  a.bias = bias;
+  a.alpha = al;
+  a.beta = be;
+  a.act = activation;
+  return from_cuda(grx::launch_conv2d_direct(a, ctx.dev.num_sms, ctx.stream));
+}
+
+grxdnnStatus_t grxdnnPoolingOutputDims(const grxdnnPoolDesc_t* d, int* p, int* q) {
+  if (!d || !p || !q) return GRXDNN_STATUS_INVALID_VALUE;
+  grxdnnConvDesc_t c{};
+  c.h = d->h; c.w = d->w; c.r = d->r; c.s = d->s; c.padH = d->padH; c.padW = d->padW;
+  c.strideH = d->strideH; c.strideW = d->strideW; c.dilationH = 1; c.dilationW = 1;
+  return grxdnnConvOutputDims(&c, p, q);
+}
+
+grxdnnStatus_t grxdnnPooling2dForward(grxdnnHandle_t handle, const grxdnnPoolDesc_t* d, const void* x,
+                                      grxDataType_t xType, void* y, grxDataType_t yType) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (!d) return GRXDNN_STATUS_INVALID_VALUE;
+  int P = 0, Q = 0;
+  if (d->n < 0 || d->c <= 0 || (unsigned)d->mode > 2u) return GRXDNN_STATUS_INVALID_VALUE;
+  grxdnnStatus_t s = grxdnnPoolingOutputDims(d, &P, &Q);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  if (d->n == 0) return GRXDNN_STATUS_SUCCESS;
+  if (!x || !y) return GRXDNN_STATUS_INVALID_VALUE;
+  if (xType != yType || norm_dtype(xType) < 0) return GRXDNN_STATUS_NOT_SUPPORTED;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  s = ensure(ctx, false);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  grx::PoolArgs a{};
+  a.n = d->n; a.h = d->h; a.w = d->w; a.c = d->c; a.r = d->r; a.s = d->s; a.p = P; a.q = Q;
+  a.pad_h = d->padH; a.pad_w = d->padW; a.stride_h = d->strideH; a.stride_w = d->strideW;
+  a.mode = (int)d->mode;
+  a.dtype = norm_dtype(xType);
+  a.x = x;
+  a.y = y;
+  return from_cuda(grx::launch_pool2d(a, ctx.dev.num_sms, ctx.stream));
 }
 
 grxdnnStatus_t grxdnnGetExecutionStatus(grxdnnHandle_t handle) {

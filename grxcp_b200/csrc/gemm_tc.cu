@@ -171,6 +171,16 @@ __device__ __noinline__ void sk_store_partial(const TcGemmParams& p, uint32_t t_
   }
 }
 
+// Output-pixel block of conv n-tile nt: image, first row, first column.
+__device__ __forceinline__ void conv_tile(const TcGemmParams& p, int nt, int& img, int& p0, int& q0) {
+  const int per_img = p.cv_tiles_p * p.cv_tiles_q;
+  img = nt / per_img;
+  const int rem = nt - img * per_img;
+  const int tp = rem / p.cv_tiles_q;
+  p0 = tp * p.cv_th;
+  q0 = (rem - tp * p.cv_tiles_q) * p.cv_tw;
+}
+
 // Waits without honouring the abort flag: used only to let in-flight copies
 // and MMAs land before the CTA releases its shared memory and TMEM.
 static __device__ __noinline__ void wait_drain(uint64_t* bar, uint32_t parity, uint64_t timeout_ns, int* err) {
@@ -371,6 +381,37 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_
   }
 }
 
+// Conv epilogue: thread = output channel i, tile column j = output pixel;
+// for each pixel the 32 lanes of a warp write 32 consecutive channels of one
+// NHWC pixel (coalesced). Pixels past the image edge are skipped.
+template <int KIND, int OUT>
+__device__ __forceinline__ void epilogue_conv(const TcGemmParams& p, uint32_t t_row, int i, int nt, int cb) {
+  int img, p0, q0;
+  conv_tile(p, nt, img, p0, q0);
+  const bool row_ok = i < p.m;
+  const float* bias_f = static_cast<const float*>(p.bias);
+  const float bias_row = (p.bias && row_ok) ? bias_f[i] : 0.f;
+  for (int c0 = cb; c0 < cb + kTileN / 2; c0 += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(t_row + c0, r);
+    tmem_ld_wait_regs(r);
+    if (!row_ok) continue;
+#pragma unroll
+    for (int jj = 0; jj < 32; ++jj) {
+      const int j = c0 + jj;
+      const int dp = j / p.cv_tw;
+      const int pp = p0 + dp, qq = q0 + (j - dp * p.cv_tw);
+      if (pp < p.cv_p && qq < p.cv_q) {
+        const long long idx = (((long long)img * p.cv_p + pp) * p.cv_q + qq) * p.ldc + i;
+        float v = __fmul_rn(p.alpha, __uint_as_float(r[jj]));
+        if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
+        if (p.bias) v = __fadd_rn(v, bias_row);
+        store_c<OUT>(p.c, idx, apply_act(v, p.act));
+      }
+    }
+  }
+}
+
 template <int KIND, int OUT>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -461,7 +502,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int j = 0; j < kTileM / ATOM; ++j)
               tma_load_3d(a_dst + j * (BK * 128), &tmA, fb, mt * kTileM + j * ATOM, k0, ba);
           }
-          if (!p.b_mn_major) {
+          if (p.conv) {
+            // k-block kb = (filter tap r s, 64-channel block); the box of
+            // cv_th x cv_tw output pixels reads input rows/columns at the
+            // conv strides, and out-of-range (padding) coordinates read 0.
+            const int rs = kb / p.cv_cb;
+            const int c0 = (kb - rs * p.cv_cb) * 64;
+            const int fr = rs / p.cv_s, fs = rs - fr * p.cv_s;
+            int img, p0, q0;
+            conv_tile(p, nt, img, p0, q0);
+            tma_load_4d(b_dst, &tmB, fb, c0, q0 * p.cv_sw - p.cv_pw + fs * p.cv_dw,
+                        p0 * p.cv_sh - p.cv_ph + fr * p.cv_dh, img);
+          } else if (!p.b_mn_major) {
             tma_load_3d(b_dst, &tmB, fb, k0, nt * kTileN, bb);
           } else {
 #pragma unroll
@@ -538,7 +590,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int bt, mt, nt;
       decode_tile(p, t, bt, mt, nt);
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + b * kTileN;
-      if (split < 0) {
+      if (p.conv) {
+        epilogue_conv<KIND, OUT>(p, t_row, mt * kTileM + row, nt, cb);
+      } else if (split < 0) {
         epilogue_tile<KIND, OUT>(p, t_row, bt, mt * kTileM + row, nt * kTileN, cb);
       } else {
         // A cut tile: publish this unit's partial, count it in, and let the
@@ -968,6 +1022,78 @@ size_t tc_gemm_splitk_bytes(int kind, int m, int n, int k, int batch, int num_sm
   const long long tiles = (long long)((m + kTileM - 1) / kTileM) * ((n + kTileN - 1) / kTileN) * batch;
   SkPlan sp;
   return plan_splitk(tiles, (k + bk - 1) / bk, num_sms, sp) ? splitk_bytes(sp) : 0;
+}
+
+// NHWC bf16 input as a 4-D map {c, w, h, n}: box {64 channels, tw * sw
+// columns, th * sh rows, 1 image} with traversal strides {1, sw, sh, 1}, so a
+// load returns th x tw pixels x 64 channels, 128 bytes per pixel row of the
+// 128-byte swizzle.
+static bool make_conv_map(CUtensorMap* map, const void* x, int n, int h, int w, int c, int th, int tw, int sh,
+                          int sw) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return false;
+  cuuint64_t dims[4] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
+  cuuint64_t strides[3] = {(cuuint64_t)c * 2, (cuuint64_t)w * c * 2, (cuuint64_t)h * w * c * 2};
+  cuuint32_t box[4] = {64, (cuuint32_t)(tw * sw), (cuuint32_t)(th * sh), 1};
+  cuuint32_t estr[4] = {1, (cuuint32_t)sw, (cuuint32_t)sh, 1};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(x), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t launch_tc_conv(const TcConvLaunch& L, int num_sms, cudaStream_t stream) {
+  if (L.c % 64 || (reinterpret_cast<uintptr_t>(L.x) & 15u) || (reinterpret_cast<uintptr_t>(L.w) & 15u))
+    return cudaErrorNotSupported;
+  if (L.stride_h < 1 || L.stride_w < 1 || L.stride_h > 8 || L.stride_w > 8) return cudaErrorNotSupported;
+  // Pixel block: tw the power of two covering the output width (capped so the
+  // strided box stays within 256), th = 256 / tw.
+  int tw = 1;
+  while (tw < L.q && tw < 256) tw <<= 1;
+  while (tw * L.stride_w > 256) tw >>= 1;
+  int th = kTileN / tw;
+  if (th * L.stride_h > 256) return cudaErrorNotSupported;
+  TcGemmParams p = L.p_epi;
+  p.abi_version = kTcGemmAbi;
+  p.conv = 1;
+  p.m = L.k;
+  p.k = L.r * L.s * L.c;
+  p.batch = 1;
+  p.cv_p = L.p;
+  p.cv_q = L.q;
+  p.cv_th = th;
+  p.cv_tw = tw;
+  p.cv_tiles_p = (L.p + th - 1) / th;
+  p.cv_tiles_q = (L.q + tw - 1) / tw;
+  p.cv_sh = L.stride_h;
+  p.cv_sw = L.stride_w;
+  p.cv_ph = L.pad_h;
+  p.cv_pw = L.pad_w;
+  p.cv_dh = L.dil_h;
+  p.cv_dw = L.dil_w;
+  p.cv_s = L.s;
+  p.cv_cb = L.c / 64;
+  p.n = L.n * L.p * L.q;
+  p.m_tiles = (L.k + kTileM - 1) / kTileM;
+  const long long n_tiles = (long long)L.n * p.cv_tiles_p * p.cv_tiles_q;
+  const long long tiles = n_tiles * p.m_tiles;
+  if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
+  p.n_tiles = (int)n_tiles;
+  p.k_blocks = p.k / 64;
+  if (p.group_m <= 0) p.group_m = 16;
+  p.a_mn_major = 0;
+  p.b_mn_major = 0;
+  p.a_batch_step = p.b_batch_step = 0;
+  p.idesc = make_idesc(1u, 1u, 1u, 0u, 0u, kTileM, kTileN);
+  p.sk_dp_tiles = (int)tiles;
+  p.sk_tiles = 0;
+  p.sk_splits = 1;
+  CUtensorMap ma, mb;
+  if (!make_operand_map(&ma, L.w, 2, 0, L.k, p.k, p.k, 0, 1, 128)) return cudaErrorNotSupported;
+  if (!make_conv_map(&mb, L.x, L.n, L.h, L.wd, L.c, th, tw, L.stride_h, L.stride_w)) return cudaErrorNotSupported;
+  const int grid = (int)(tiles < num_sms ? tiles : num_sms);
+  if (L.out == kOutBF16) return launch_impl<kKindF16, kOutBF16>(ma, mb, p, grid, stream);
+  if (L.out == kOutF32) return launch_impl<kKindF16, kOutF32>(ma, mb, p, grid, stream);
+  return cudaErrorNotSupported;
 }
 
 cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stream) {

@@ -11,7 +11,7 @@ namespace grx {
 // The kernel refuses to run on a version mismatch (the reference's kernel ABI
 // blocks do the same, src/libs/grxblas/hgemm_abi.h:20 and
 // src/libs/grxblas/kernels/sgemm.cpp:23-27).
-constexpr uint32_t kTcGemmAbi = 4;
+constexpr uint32_t kTcGemmAbi = 5;
 
 enum TcKind : int { kKindF16 = 0, kKindI8 = 1, kKindF8 = 2 };
 enum TcOut : int { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2, kOutS32 = 3 };
@@ -51,6 +51,13 @@ struct TcGemmParams {
   int sk_splits;
   uint32_t* sk_part;
   int* sk_count;
+  // Implicit-GEMM conv2d (conv != 0): op(A) is the K x (R S C) filter matrix,
+  // op(B) the im2col of an NHWC input read by 4-D TMA loads, and tile column j
+  // of n-tile nt is output pixel (img, p0 + j / cv_tw, q0 + j % cv_tw) of a
+  // cv_th x cv_tw block (cv_th * cv_tw = kTileN); C is NHWC (ldc = K).
+  int conv;
+  int cv_p, cv_q, cv_th, cv_tw, cv_tiles_p, cv_tiles_q;
+  int cv_sh, cv_sw, cv_ph, cv_pw, cv_dh, cv_dw, cv_s, cv_cb;
 };
 
 struct TcGemmLaunch {
@@ -94,6 +101,20 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
 // Bytes of scratch the split-K tail of this problem wants (0: the problem
 // runs as whole tiles). The decision matches launch_tc_gemm's.
 size_t tc_gemm_splitk_bytes(int kind, int m, int n, int k, int batch, int num_sms);
+
+// Implicit-GEMM conv2d on the tcgen05 kernel: x NHWC bf16 [n, h, w, c],
+// filters KRSC bf16 [k, r, s, c], y NHWC [n, p, q, k] (bf16 or fp32 by out).
+// Requires c % 64 == 0 and 16-byte aligned x / w. Epilogue: alpha, beta * y,
+// bias over output channels (p.bias, bias_rows = 1) and p.act.
+struct TcConvLaunch {
+  int out;  // TcOut: kOutBF16 or kOutF32
+  const void* x;
+  const void* w;
+  int n, h, wd, c, k, r, s, p, q;
+  int pad_h, pad_w, stride_h, stride_w, dil_h, dil_w;
+  TcGemmParams p_epi;  // alpha, beta, c, ldc, bias, act, err_word, timeout_ns
+};
+cudaError_t launch_tc_conv(const TcConvLaunch& L, int num_sms, cudaStream_t stream);
 
 // True when an operand can be fed to TMA as stored.
 bool tma_operand_ok(const void* base, long long ld, long long stride, int elem_bytes, int batch);

@@ -47,6 +47,30 @@ cudaError_t launch_layernorm(int rows, int hidden, int dtype, const void* x, lon
 
 // Softmax over each row / element-wise activation (softmax.cu); dtype as norms,
 // act a grx::kAct* value.
+// conv2d direct fallback and pooling (conv.cu), NHWC activations, KRSC
+// filters. dtype codes: 0 f32, 1 bf16, 2 f16.
+struct ConvArgs {
+  int n, h, w, c, k, r, s, p, q;
+  int pad_h, pad_w, stride_h, stride_w, dil_h, dil_w;
+  int in_dtype, out_dtype;
+  const void* x;
+  const void* filt;
+  void* y;
+  const float* bias;
+  float alpha, beta;
+  int act;
+};
+cudaError_t launch_conv2d_direct(const ConvArgs& a, int num_sms, cudaStream_t s);
+struct PoolArgs {
+  int n, h, w, c, r, s, p, q;
+  int pad_h, pad_w, stride_h, stride_w;
+  int mode;  // 0 max, 1 average over r*s, 2 average over in-image taps
+  int dtype;
+  const void* x;
+  void* y;
+};
+cudaError_t launch_pool2d(const PoolArgs& a, int num_sms, cudaStream_t s);
+
 // RMSNorm / LayerNorm backward (norm_bwd.cu). mean/rstd: saved statistics
 // or null (recomputed); dgamma/dbeta may be null. ws: scratch of at least
 // norm_bwd_workspace_bytes when dgamma/dbeta are wanted or stats are null.

@@ -1,4 +1,4 @@
-"""grxDNN from Python: RMSNorm, LayerNorm and fused attention forward.
+"""grxDNN from Python: norms (forward and backward), softmax, GELU, conv2d, pooling and attention (forward and backward).
 
 Thin mirror of include/grx/grxdnn.h; every method returns the raw status code
 of the C call. Tensors are torch CUDA tensors (or integer device addresses).
@@ -39,6 +39,25 @@ def attn_desc(t, batch=None, heads=None, seq=None, head_dim=None, dtype=None) ->
         d.strideBatch, d.strideHead, d.strideSeq = heads * seq * head_dim, seq * head_dim, head_dim
         d.dtype = dtype if dtype is not None else N.GRX_R_16BF
     return d
+
+
+def conv_desc(x, w, pad=(0, 0), stride=(1, 1), dilation=(1, 1)):
+    n, h, wd, c = x.shape
+    k, r, s, _ = w.shape
+    return N.grxdnnConvDesc_t(n, h, wd, c, k, r, s, pad[0], pad[1], stride[0], stride[1], dilation[0], dilation[1])
+
+
+def conv_out_dims(d) -> tuple[int, int]:
+    p, q = C.c_int(), C.c_int()
+    st = lib.grxdnnConvOutputDims(C.byref(d), C.byref(p), C.byref(q))
+    if st != 0:
+        raise ValueError(f"bad conv geometry (status {st})")
+    return p.value, q.value
+
+
+def pool_desc(x, window, pad=(0, 0), stride=(1, 1), mode=0):
+    n, h, wd, c = x.shape
+    return N.grxdnnPoolDesc_t(n, h, wd, c, window[0], window[1], pad[0], pad[1], stride[0], stride[1], mode)
 
 
 class Handle:
@@ -121,6 +140,21 @@ class Handle:
                                            ptr(v), C.byref(ds[3]), ptr(o), C.byref(ds[4]), ptr(dout), ptr(lse),
                                            scale, 1 if causal else 0, C.byref(ds[5]), ptr(dq), C.byref(ds[6]),
                                            ptr(dk), C.byref(ds[7]), ptr(dv))
+
+    def conv2d(self, x, w, y, pad=(0, 0), stride=(1, 1), dilation=(1, 1), bias=None, activation=0, alpha=None,
+               beta=None) -> int:
+        """grxdnnConv2dForward: x [n, h, w, c] NHWC, w [k, r, s, c] KRSC, y [n, p, q, k]."""
+        d = conv_desc(x, w, pad, stride, dilation)
+        a = C.c_float(alpha) if alpha is not None else None
+        b = C.c_float(beta) if beta is not None else None
+        return lib.grxdnnConv2dForward(self.h, C.byref(d), ptr(x), dtype_code(x), ptr(w), dtype_code(w),
+                                       C.byref(a) if a is not None else None, C.byref(b) if b is not None else None,
+                                       ptr(bias), activation, ptr(y), dtype_code(y))
+
+    def pool2d(self, x, y, window, pad=(0, 0), stride=None, mode=0) -> int:
+        """grxdnnPooling2dForward on NHWC tensors."""
+        d = pool_desc(x, window, pad, stride or window, mode)
+        return lib.grxdnnPooling2dForward(self.h, C.byref(d), ptr(x), dtype_code(x), ptr(y), dtype_code(y))
 
     def attention(self, q, k, v, o, scale, causal, lse=None, descs=None) -> int:
         dq, dk, dv, do = descs if descs is not None else (attn_desc(q), attn_desc(k), attn_desc(v), attn_desc(o))

@@ -153,6 +153,54 @@ grxdnnStatus_t grxdnnAttentionBackward(grxdnnHandle_t handle,
                                        const grxdnnAttnTensor_t* dKDesc, void* dK,
                                        const grxdnnAttnTensor_t* dVDesc, void* dV);
 
+/* 2-D convolution (planned in the reference's grxDNN as "conv2d (implicit
+ * GEMM)", never implemented there): NHWC input x [n, h, w, c], KRSC filters
+ * [k, r, s, c], NHWC output y [n, p, q, k] with
+ *   p = (h + 2 padH - dilationH (r - 1) - 1) / strideH + 1   (q likewise),
+ *   y = act(alpha * conv(x, w) + beta * y + bias[k]).
+ * alpha / beta are host pointers (NULL: 1 / 0; beta == 0 never reads y).
+ * bias (fp32 [k]) may be NULL; activation as grxblasActivation_t (0 none,
+ * 1 ReLU, 2 GELU tanh, 3 GELU erf). Types: x and w both GRX_R_16BF (y bf16 or
+ * fp32) or both GRX_R_32F (y fp32). bf16 with c a multiple of 64 runs as an
+ * implicit GEMM on the tensor cores; other shapes run a direct kernel. */
+typedef struct {
+  int n, h, w, c;
+  int k, r, s;
+  int padH, padW, strideH, strideW, dilationH, dilationW;
+} grxdnnConvDesc_t;
+
+grxdnnStatus_t grxdnnConvOutputDims(const grxdnnConvDesc_t* desc, int* p, int* q);
+grxdnnStatus_t grxdnnConv2dForward(grxdnnHandle_t handle, const grxdnnConvDesc_t* desc,
+                                   const void* x, grxDataType_t xType,
+                                   const void* w, grxDataType_t wType,
+                                   const float* alpha, const float* beta,
+                                   const float* bias, int activation,
+                                   void* y, grxDataType_t yType);
+
+/* 2-D pooling over NHWC (planned in the reference's grxDNN, never
+ * implemented): windows r x s at the given strides and zero-based padding;
+ * MAX (a window wholly in the padding gives 0), AVG_INCLUDE_PAD (divide by
+ * r s) or AVG_EXCLUDE_PAD (divide by the in-image taps). x and y share one
+ * type (GRX_R_16BF, GRX_R_16F, GRX_R_32F); y is [n, p, q, c] with p, q as
+ * for conv with dilation 1. */
+typedef enum {
+  GRXDNN_POOL_MAX = 0,
+  GRXDNN_POOL_AVG_INCLUDE_PAD = 1,
+  GRXDNN_POOL_AVG_EXCLUDE_PAD = 2
+} grxdnnPoolMode_t;
+
+typedef struct {
+  int n, h, w, c;
+  int r, s;
+  int padH, padW, strideH, strideW;
+  grxdnnPoolMode_t mode;
+} grxdnnPoolDesc_t;
+
+grxdnnStatus_t grxdnnPoolingOutputDims(const grxdnnPoolDesc_t* desc, int* p, int* q);
+grxdnnStatus_t grxdnnPooling2dForward(grxdnnHandle_t handle, const grxdnnPoolDesc_t* desc,
+                                      const void* x, grxDataType_t xType,
+                                      void* y, grxDataType_t yType);
+
 grxdnnStatus_t grxdnnGetExecutionStatus(grxdnnHandle_t handle);
 
 #ifdef __cplusplus

@@ -67,6 +67,7 @@ _protos = {
     "ora_norm_bwd": (None, [_i, _i, _i, _vp, _vp, _vp, _d, _vp, _vp, _vp]),
     "ora_layernorm": (None, [_i, _i, _vp, _ll, _vp, _vp, _d, _vp, _vp, _vp, _i]),
     "ora_attention": (None, [_i, _i, _i, _i, _vp, _vp, _vp, _d, _i, _vp, _i, _i, _i, _vp, _vp, _i]),
+    "ora_conv2d": (None, [_i] * 15 + [_vp, _vp, _vp]),
     "ora_attention_bwd": (None, [_i, _i, _i, _i, _vp, _vp, _vp, _vp, _d, _i, _vp, _vp, _vp, _i]),
     "ora_saxpy": (None, [_i, _f, _vp, _i, _vp, _i]),
     "ora_softmax": (None, [_i, _i, _vp, _ll, _vp]),
@@ -242,6 +243,46 @@ def attention_bwd(q, k, v, dout, scale, causal, nthreads=None):
     _lib.ora_attention_bwd(BH, Sq, Sk, D, _p(q), _p(k), _p(v), _p(dout), scale, int(causal), _p(dq), _p(dk), _p(dv),
                            nthreads or nthreads_default())
     return dq, dk, dv
+
+
+def conv2d(x, w, pad=(0, 0), stride=(1, 1), dilation=(1, 1)):
+    """fp64 conv2d: x [n, h, w, c] NHWC, w [k, r, s, c] KRSC -> y [n, p, q, k]."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    n, h, wd, c = x.shape
+    k, r, s, _ = w.shape
+    P = (h + 2 * pad[0] - dilation[0] * (r - 1) - 1) // stride[0] + 1
+    Q = (wd + 2 * pad[1] - dilation[1] * (s - 1) - 1) // stride[1] + 1
+    y = np.empty((n, P, Q, k), np.float64)
+    _lib.ora_conv2d(n, h, wd, c, k, r, s, pad[0], pad[1], stride[0], stride[1], dilation[0], dilation[1], P, Q, _p(x),
+                    _p(w), _p(y))
+    return y
+
+
+def pool2d(x, window, pad=(0, 0), stride=None, mode=0):
+    """fp64 NHWC pooling: mode 0 max (0 for an all-padding window), 1 average over r*s,
+    2 average over the in-image taps."""
+    x = np.asarray(x, np.float64)
+    n, h, wd, c = x.shape
+    r, s = window
+    st = stride or window
+    P = (h + 2 * pad[0] - r) // st[0] + 1
+    Q = (wd + 2 * pad[1] - s) // st[1] + 1
+    y = np.zeros((n, P, Q, c))
+    for p in range(P):
+        for q in range(Q):
+            h0, w0 = p * st[0] - pad[0], q * st[1] - pad[1]
+            win = x[:, max(h0, 0):min(h0 + r, h), max(w0, 0):min(w0 + s, wd), :]
+            cnt = win.shape[1] * win.shape[2]
+            if cnt == 0:
+                continue
+            if mode == 0:
+                y[:, p, q, :] = win.max(axis=(1, 2))
+            elif mode == 1:
+                y[:, p, q, :] = win.sum(axis=(1, 2)) / (r * s)
+            else:
+                y[:, p, q, :] = win.sum(axis=(1, 2)) / cnt
+    return y
 
 
 # ------------------------------------------------------------ level 1 / 2

@@ -559,6 +559,31 @@ void ora_attention_bwd(int BH, int Sq, int Sk, int D, const float* q, const floa
   free(th);
 }
 
+/* conv2d in fp64 (NHWC x, KRSC w, NHWC y; no reference code exists): the
+ * definition y[n,p,q,k] = sum_{r,s,c} x[n, p sh - ph + r dh, q sw - pw + s dw, c]
+ * w[k,r,s,c], taps outside the image contributing 0. */
+void ora_conv2d(int n, int h, int w, int c, int k, int r, int s, int ph, int pw, int sh, int sw, int dh, int dw,
+                int P, int Q, const float* x, const float* f, double* y) {
+  for (int ni = 0; ni < n; ++ni)
+    for (int p = 0; p < P; ++p)
+      for (int q = 0; q < Q; ++q)
+        for (int ki = 0; ki < k; ++ki) {
+          double acc = 0.0;
+          for (int ri = 0; ri < r; ++ri) {
+            const int hh = p * sh - ph + ri * dh;
+            if (hh < 0 || hh >= h) continue;
+            for (int si = 0; si < s; ++si) {
+              const int ww = q * sw - pw + si * dw;
+              if (ww < 0 || ww >= w) continue;
+              const float* xr = x + (((long long)ni * h + hh) * w + ww) * c;
+              const float* fr = f + (((long long)ki * r + ri) * s + si) * c;
+              for (int ci = 0; ci < c; ++ci) acc += (double)xr[ci] * (double)fr[ci];
+            }
+          }
+          y[(((long long)ni * P + p) * Q + q) * k + ki] = acc;
+        }
+}
+
 /* ------------------------------------------------------------ level 1 / 2 */
 
 /* BLAS increment addressing (tests/libs/test_grxblas_l12.cpp:27-31). */

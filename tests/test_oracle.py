@@ -256,3 +256,28 @@ def test_attention_backward_oracle_matches_autograd(causal, sq, sk):
     (torch.softmax(s, -1) @ V).backward(torch.tensor(do, dtype=torch.float64))
     for got, ref in ((dq, Q.grad), (dk, K.grad), (dv, V.grad)):
         assert np.allclose(got, ref.numpy(), rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("pad,stride,dil", [((0, 0), (1, 1), (1, 1)), ((1, 2), (2, 1), (1, 2))])
+def test_conv2d_oracle_matches_torch(pad, stride, dil):
+    """The fp64 conv restatement (NHWC / KRSC) against torch's conv2d in fp64 (NCHW)."""
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((2, 9, 11, 5)).astype(np.float32)
+    w = rng.standard_normal((4, 3, 2, 5)).astype(np.float32)
+    y = oracle.conv2d(x, w, pad, stride, dil)
+    ref = torch.nn.functional.conv2d(torch.tensor(x, dtype=torch.float64).permute(0, 3, 1, 2),
+                                     torch.tensor(w, dtype=torch.float64).permute(0, 3, 1, 2),
+                                     stride=stride, padding=pad, dilation=dil).permute(0, 2, 3, 1).numpy()
+    assert y.shape == ref.shape and np.allclose(y, ref, rtol=1e-12, atol=1e-12)
+
+
+def test_pool2d_oracle_matches_torch():
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((2, 9, 10, 3))
+    t = torch.tensor(x).permute(0, 3, 1, 2)
+    mx = torch.nn.functional.max_pool2d(t, 3, 2, 1).permute(0, 2, 3, 1).numpy()
+    av = torch.nn.functional.avg_pool2d(t, 3, 2, 1, count_include_pad=True).permute(0, 2, 3, 1).numpy()
+    ex = torch.nn.functional.avg_pool2d(t, 3, 2, 1, count_include_pad=False).permute(0, 2, 3, 1).numpy()
+    assert np.allclose(oracle.pool2d(x, (3, 3), (1, 1), (2, 2), 0), mx)
+    assert np.allclose(oracle.pool2d(x, (3, 3), (1, 1), (2, 2), 1), av)
+    assert np.allclose(oracle.pool2d(x, (3, 3), (1, 1), (2, 2), 2), ex)
