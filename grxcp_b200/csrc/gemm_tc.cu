@@ -250,12 +250,15 @@ struct EpiRow {
   bool row_ok, pair_ok;
 };
 
-template <int KIND, int OUT>
+// ncol: how many of the chunk's 32 columns exist (the rest are not stored).
+// MASKED: the pair-store path takes partial chunks too (conv); otherwise it
+// takes full chunks only and partial ones go element by element (GEMM).
+template <int KIND, int OUT, bool MASKED = false>
 __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& er, uint32_t (&r)[32], int jbase,
-                                          float sb_l, float bias_l, const float* sb, const float* bias_f,
+                                          int ncol, float sb_l, float bias_l, const float* sb, const float* bias_f,
                                           const __nv_bfloat16* bias_h) {
   const int lane = threadIdx.x & 31;
-  if (er.pair_ok && jbase + 32 <= p.n) {
+  if (er.pair_ok && (MASKED || ncol == 32)) {
     const bool odd = lane & 1;
     // even lane: rows (i, i+1) of columns jbase+jj; odd lane: rows (i-1, i) of jbase+jj+1
     const long long base = er.cbase - (odd ? 1 : 0) + (long long)(jbase + (odd ? 1 : 0)) * p.ldc;
@@ -266,7 +269,8 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& e
       for (int jj = 0; jj < 32; jj += 2) {
         const int a = p.ialpha * (int)r[jj], b = p.ialpha * (int)r[jj + 1];
         const int other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
-        *reinterpret_cast<int2*>(cp) = odd ? make_int2(other, b) : make_int2(a, other);
+        if (!MASKED || jj + (odd ? 1 : 0) < ncol)
+          *reinterpret_cast<int2*>(cp) = odd ? make_int2(other, b) : make_int2(a, other);
         cp += step;
       }
     } else {
@@ -299,6 +303,7 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& e
         const float other = __shfl_xor_sync(0xffffffffu, odd ? a : b, 1);
         const float lo = odd ? other : a, hi = odd ? b : other;  // lower row first
         const long long off = base + (long long)(jj / 2) * step;
+        if (MASKED && jj + (odd ? 1 : 0) >= ncol) continue;
         if constexpr (OUT == kOutF32) {
           *reinterpret_cast<float2*>(static_cast<float*>(p.c) + off) = make_float2(lo, hi);
         } else if constexpr (OUT == kOutBF16) {
@@ -314,7 +319,7 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& e
 #pragma unroll
   for (int jj = 0; jj < 32; ++jj) {
     const int j = jbase + jj;
-    if (j < p.n) {
+    if (jj < ncol) {
       const long long idx = er.cbase + (long long)j * p.ldc;
       if constexpr (OUT == kOutS32) {
         int v = p.ialpha * (int)r[jj];
@@ -371,48 +376,59 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_
     if (ci >= nch) break;
     tmem_ld_wait_regs(ra);
     if (ci + 1 < nch) tmem_ld_32x32b_x32(t_row + cb + (ci + 1) * 32, rb);
-    epi_chunk<KIND, OUT>(p, er, ra, col0 + cb + ci * 32, sb_pre[ci], bias_pre[ci], sb, bias_f, bias_h);
+    epi_chunk<KIND, OUT>(p, er, ra, col0 + cb + ci * 32, min(32, p.n - (col0 + cb + ci * 32)), sb_pre[ci],
+                         bias_pre[ci], sb, bias_f, bias_h);
     if (ci + 1 < nch) {
       tmem_ld_wait_regs(rb);
       if (ci + 2 < nch) tmem_ld_32x32b_x32(t_row + cb + (ci + 2) * 32, ra);
-      epi_chunk<KIND, OUT>(p, er, rb, col0 + cb + (ci + 1) * 32, sb_pre[ci + 1], bias_pre[ci + 1], sb, bias_f,
-                           bias_h);
+      epi_chunk<KIND, OUT>(p, er, rb, col0 + cb + (ci + 1) * 32, min(32, p.n - (col0 + cb + (ci + 1) * 32)),
+                           sb_pre[ci + 1], bias_pre[ci + 1], sb, bias_f, bias_h);
     }
   }
 }
 
-// Conv epilogue: thread = output channel i, tile column j = output pixel;
-// for each pixel the 32 lanes of a warp write 32 consecutive channels of one
-// NHWC pixel (coalesced). Pixels past the image edge are skipped.
+// Conv epilogue: thread = output channel i, tile column j = output pixel.
+// Full-row blocks (cv_tw == output width): the tile is one contiguous run of
+// output pixels. Wide rows (cv_tw a multiple of 32 below the output width):
+// each 32-column chunk lies in one output row. Either way a chunk is up to 32
+// consecutive NHWC pixels (stride ldc), stored through the GEMM chunk path
+// with pair stores over adjacent channels.
 template <int KIND, int OUT>
 __device__ __forceinline__ void epilogue_conv(const TcGemmParams& p, uint32_t t_row, int i, int nt, int cb) {
+  constexpr int kOutBytes = (OUT == kOutBF16 || OUT == kOutF16) ? 2 : 4;
   int img, p0, q0;
   conv_tile(p, nt, img, p0, q0);
-  const bool row_ok = i < p.m;
   const float* bias_f = static_cast<const float*>(p.bias);
-  const float bias_row = (p.bias && row_ok) ? bias_f[i] : 0.f;
+  EpiRow er;
+  er.row_ok = i < p.m;
+  er.rowmul = p.alpha;
+  er.bias_row = (p.bias && er.row_ok) ? bias_f[i] : 0.f;
+  const int i_warp0 = __shfl_sync(0xffffffffu, i, 0);
+  er.pair_ok = !p.beta_nonzero && (p.ldc % 2 == 0) && (i_warp0 % 2 == 0) &&
+               ((reinterpret_cast<uintptr_t>(p.c) % (2 * kOutBytes)) == 0) && i_warp0 + 31 < p.m;
+  const int rows_here = min(p.cv_th, p.cv_p - p0);
   for (int c0 = cb; c0 < cb + kTileN / 2; c0 += 32) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(t_row + c0, r);
     tmem_ld_wait_regs(r);
-    if (!row_ok) continue;
-#pragma unroll
-    for (int jj = 0; jj < 32; ++jj) {
-      const int j = c0 + jj;
-      const int dp = j / p.cv_tw;
-      const int pp = p0 + dp, qq = q0 + (j - dp * p.cv_tw);
-      if (pp < p.cv_p && qq < p.cv_q) {
-        const long long idx = (((long long)img * p.cv_p + pp) * p.cv_q + qq) * p.ldc + i;
-        float v = __fmul_rn(p.alpha, __uint_as_float(r[jj]));
-        if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
-        if (p.bias) v = __fadd_rn(v, bias_row);
-        store_c<OUT>(p.c, idx, apply_act(v, p.act));
-      }
+    int ncol;
+    long long pix;
+    if (p.cv_tw == p.cv_q) {
+      ncol = min(32, rows_here * p.cv_q - c0);
+      pix = ((long long)img * p.cv_p + p0) * p.cv_q + c0;
+    } else {
+      const int dp = c0 / p.cv_tw;
+      const int qq = q0 + (c0 - dp * p.cv_tw);
+      ncol = dp < rows_here ? min(32, p.cv_q - qq) : 0;
+      pix = ((long long)img * p.cv_p + p0 + dp) * p.cv_q + qq;
     }
+    if (ncol <= 0) continue;  // warp-uniform
+    er.cbase = pix * p.ldc + i;
+    epi_chunk<KIND, OUT, true>(p, er, r, 0, ncol, 1.f, 0.f, nullptr, bias_f, nullptr);
   }
 }
 
-template <int KIND, int OUT>
+template <int KIND, int OUT, bool CONV>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ TcGemmParams p) {
@@ -489,7 +505,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           uint64_t* fb = &full[stage];
-          mbar_arrive_expect_tx(fb, kStageTx);
+          mbar_arrive_expect_tx(fb, CONV ? (uint32_t)kStageBytesA + p.cv_b_bytes : kStageTx);
           issued_mask |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
           uint8_t* a_dst = sA + stage * kStageBytesA;
@@ -502,7 +518,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int j = 0; j < kTileM / ATOM; ++j)
               tma_load_3d(a_dst + j * (BK * 128), &tmA, fb, mt * kTileM + j * ATOM, k0, ba);
           }
-          if (p.conv) {
+          if constexpr (CONV) {
             // k-block kb = (filter tap r s, 64-channel block); the box of
             // cv_th x cv_tw output pixels reads input rows/columns at the
             // conv strides, and out-of-range (padding) coordinates read 0.
@@ -590,7 +606,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int bt, mt, nt;
       decode_tile(p, t, bt, mt, nt);
       const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + b * kTileN;
-      if (p.conv) {
+      if constexpr (CONV) {
         epilogue_conv<KIND, OUT>(p, t_row, mt * kTileM + row, nt, cb);
       } else if (split < 0) {
         epilogue_tile<KIND, OUT>(p, t_row, bt, mt * kTileM + row, nt * kTileN, cb);
@@ -902,10 +918,10 @@ static bool make_operand_map(CUtensorMap* map, const void* base, int es, int mn_
   return r == CUDA_SUCCESS;
 }
 
-template <int KIND, int OUT>
+template <int KIND, int OUT, bool CONV = false>
 static cudaError_t launch_impl(const CUtensorMap& ma, const CUtensorMap& mb, const TcGemmParams& p, int grid,
                                cudaStream_t s) {
-  auto kfn = tc_gemm_kernel<KIND, OUT>;
+  auto kfn = tc_gemm_kernel<KIND, OUT, CONV>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -1045,13 +1061,21 @@ cudaError_t launch_tc_conv(const TcConvLaunch& L, int num_sms, cudaStream_t stre
   if (L.c % 64 || (reinterpret_cast<uintptr_t>(L.x) & 15u) || (reinterpret_cast<uintptr_t>(L.w) & 15u))
     return cudaErrorNotSupported;
   if (L.stride_h < 1 || L.stride_w < 1 || L.stride_h > 8 || L.stride_w > 8) return cudaErrorNotSupported;
-  // Pixel block: tw the power of two covering the output width (capped so the
-  // strided box stays within 256), th = 256 / tw.
-  int tw = 1;
-  while (tw < L.q && tw < 256) tw <<= 1;
-  while (tw * L.stride_w > 256) tw >>= 1;
-  int th = kTileN / tw;
-  if (th * L.stride_h > 256) return cudaErrorNotSupported;
+  // Pixel block of th x tw output pixels (th * tw <= kTileN columns). Whole
+  // output rows when they fit the box (tw = q, th = 256 / q): the tile is
+  // then one contiguous run of output pixels. Otherwise wide rows cut into
+  // multiples of 32 columns. Each box dimension spans at most 256 input
+  // elements (tw * stride_w, th * stride_h).
+  int tw, th;
+  if ((long long)L.q * L.stride_w <= 256) {
+    tw = L.q;
+    th = kTileN / tw;
+  } else {
+    tw = (256 / L.stride_w) & ~31;
+    th = kTileN / tw;
+  }
+  if (th * L.stride_h > 256) th = 256 / L.stride_h;
+  if (tw < 1 || th < 1) return cudaErrorNotSupported;
   TcGemmParams p = L.p_epi;
   p.abi_version = kTcGemmAbi;
   p.conv = 1;
@@ -1072,6 +1096,7 @@ cudaError_t launch_tc_conv(const TcConvLaunch& L, int num_sms, cudaStream_t stre
   p.cv_dw = L.dil_w;
   p.cv_s = L.s;
   p.cv_cb = L.c / 64;
+  p.cv_b_bytes = (uint32_t)(128 * tw * th);
   p.n = L.n * L.p * L.q;
   p.m_tiles = (L.k + kTileM - 1) / kTileM;
   const long long n_tiles = (long long)L.n * p.cv_tiles_p * p.cv_tiles_q;
@@ -1091,8 +1116,8 @@ cudaError_t launch_tc_conv(const TcConvLaunch& L, int num_sms, cudaStream_t stre
   if (!make_operand_map(&ma, L.w, 2, 0, L.k, p.k, p.k, 0, 1, 128)) return cudaErrorNotSupported;
   if (!make_conv_map(&mb, L.x, L.n, L.h, L.wd, L.c, th, tw, L.stride_h, L.stride_w)) return cudaErrorNotSupported;
   const int grid = (int)(tiles < num_sms ? tiles : num_sms);
-  if (L.out == kOutBF16) return launch_impl<kKindF16, kOutBF16>(ma, mb, p, grid, stream);
-  if (L.out == kOutF32) return launch_impl<kKindF16, kOutF32>(ma, mb, p, grid, stream);
+  if (L.out == kOutBF16) return launch_impl<kKindF16, kOutBF16, true>(ma, mb, p, grid, stream);
+  if (L.out == kOutF32) return launch_impl<kKindF16, kOutF32, true>(ma, mb, p, grid, stream);
   return cudaErrorNotSupported;
 }
 

@@ -54,10 +54,12 @@ struct TcGemmParams {
   // Implicit-GEMM conv2d (conv != 0): op(A) is the K x (R S C) filter matrix,
   // op(B) the im2col of an NHWC input read by 4-D TMA loads, and tile column j
   // of n-tile nt is output pixel (img, p0 + j / cv_tw, q0 + j % cv_tw) of a
-  // cv_th x cv_tw block (cv_th * cv_tw = kTileN); C is NHWC (ldc = K).
+  // cv_th x cv_tw block (cv_th * cv_tw <= kTileN; later columns unused); C is
+  // NHWC (ldc = K).
   int conv;
   int cv_p, cv_q, cv_th, cv_tw, cv_tiles_p, cv_tiles_q;
   int cv_sh, cv_sw, cv_ph, cv_pw, cv_dh, cv_dw, cv_s, cv_cb;
+  uint32_t cv_b_bytes;  // bytes one pixel-block box delivers (th * tw * 128)
 };
 
 struct TcGemmLaunch {
