@@ -255,9 +255,14 @@ def run_gpu(args):
             parts = line.split()
             if len(parts) == 2 and parts[0] == "gemm_bf16_8192_per_launch_bytes":
                 traffic = float(parts[1]) * nl / N  # scales with the column shard
+    # the library's choice (gemm_tc.cu use_pair): CTA pairs for 16-bit problems with at least four
+    # 256 x 256 pair-tiles per pair of SMs
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    pair = M >= 256 and nl >= 256 and -(-M // 256) * -(-nl // 256) >= 4 * (sms // 2)
+    kernel_name = "grx::tc_gemm_pair_kernel<kind::f16, bf16 out>" if pair else "grx::tc_gemm_kernel<kind::f16, bf16 out>"
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "traffic": traffic, "peak_source": f"{peaks_src} bf16_tflops (burst)",
-                "kernel": "grx::tc_gemm_kernel<bf16, bf16 out>"}
+                "kernel": kernel_name}
 
     # ---- end to end through the public API with host buffers (pinned). Every
     # step copies its inputs host -> device and its result device -> host; the
@@ -533,6 +538,33 @@ def run_profile(args):
             lse = torch.empty(8, 32, 4096, device=dev)
             for _ in range(n_iter):
                 D.check(dh.attention(q, k, v, o, 1 / math.sqrt(128), True, lse))
+        elif args.profile == "attention_bwd":
+            # config 4 per head at batch 2 (a quarter of the heads), so a capture holds ~0.5 GB
+            q = torch.randn(2, 32, 4096, 128, device=dev, generator=g).to(torch.bfloat16)
+            k, v, o, do = torch.randn_like(q), torch.randn_like(q), torch.empty_like(q), torch.randn_like(q)
+            dq, dk, dv = torch.empty_like(q), torch.empty_like(q), torch.empty_like(q)
+            lse = torch.empty(2, 32, 4096, device=dev)
+            D.check(dh.attention(q, k, v, o, 1 / math.sqrt(128), True, lse))
+            for _ in range(n_iter):
+                D.check(dh.attention_backward(q, k, v, o, do, lse, 1 / math.sqrt(128), True, dq, dk, dv))
+        elif args.profile in ("rmsnorm_bwd", "layernorm_bwd"):
+            x = torch.randn(16384, 8192, device=dev, generator=g).to(torch.bfloat16)
+            dy, dx = torch.randn_like(x), torch.empty_like(x)
+            gamma, beta = torch.ones(8192, device=dev), torch.zeros(8192, device=dev)
+            mean, rstd = torch.empty(16384, device=dev), torch.empty(16384, device=dev)
+            dgamma, dbeta = torch.empty(8192, device=dev), torch.empty(8192, device=dev)
+            D.check(dh.layernorm(x, gamma, beta, 1e-5, dx, mean, rstd))
+            for _ in range(n_iter):
+                if args.profile == "rmsnorm_bwd":
+                    D.check(dh.rmsnorm_backward(dy, x, gamma, 1e-5, dx, rstd, dgamma))
+                else:
+                    D.check(dh.layernorm_backward(dy, x, gamma, 1e-5, dx, mean, rstd, dgamma, dbeta))
+        elif args.profile == "conv":
+            x = torch.randn(128, 28, 28, 128, device=dev, generator=g).to(torch.bfloat16)
+            w = (torch.randn(128, 3, 3, 128, device=dev, generator=g) / 34).to(torch.bfloat16)
+            y = torch.empty(128, 28, 28, 128, device=dev).to(torch.bfloat16)
+            for _ in range(n_iter):
+                D.check(dh.conv2d(x, w, y, (1, 1)))
         else:
             x = torch.randn(65536, 8192, device=dev, generator=g).to(torch.bfloat16)
             y = torch.empty_like(x)
@@ -556,7 +588,8 @@ def main():
     ap.add_argument("--impl", default="grxcp", choices=["grxcp", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
-    ap.add_argument("--profile", choices=["gemm", "attention", "rmsnorm", "layernorm", "fp8"],
+    ap.add_argument("--profile", choices=["gemm", "attention", "rmsnorm", "layernorm", "fp8", "attention_bwd",
+                                          "rmsnorm_bwd", "layernorm_bwd", "conv"],
                     help="run only this kernel warmup+steps times (for ncu captures); prints no JSON")
     args = ap.parse_args()
     if args.impl == "reference":
