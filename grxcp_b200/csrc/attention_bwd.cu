@@ -17,19 +17,23 @@
 //       kernel through fp32 atomics.
 // CTA: 320 threads. Warp 0 is the TMA producer (one thread): the resident pair
 // once, then the streamed pair of each block through a 2-stage ring. Warp 1 is
-// the MMA issuer (one thread): per block S = Q K^T and dP = dO V^T (K-major
-// operands, 128 x 128 x 128 each), then dV += P^T dO and dK += dS^T Q (KV
-// kernel) or dQ += dS K (Q kernel). Warps 2..9, two per TMEM lane quadrant
-// (thread = query row; warp w takes columns [64 (w-2)/4, +64)), read S and dP
-// from TMEM 32 columns at a time, form P and dS in fp32 and
-// write them as bf16 into one 128 x 128 shared-memory tile in the same
-// 128-byte-swizzled layout TMA gives a loaded tile (rows = queries). Read
-// with a K-major descriptor that tile is the A operand for dQ (M = queries);
-// read with an MN-major descriptor it is the A operand P^T / dS^T for dV / dK
-// (M = keys). In the KV kernel the tile holds P first and dS second (dS waits
-// in registers as packed bf16 while dV reads P).
-// TMEM (512 columns): S [0,128), dP [128,256), dV or dQ [256,384), dK
-// [384,512). All waits are bounded (ptx.cuh).
+// the MMA issuer (one thread). Warps 2..9 (two per TMEM lane quadrant) form P
+// and dS. Each streamed block is worked in two halves of 64 (queries for the
+// KV kernel, keys for the Q kernel) that ping-pong: while the compute warps
+// turn half h's scores into P / dS, the tensor pipe runs the other half.
+//   KV kernel, TMEM lanes = the CTA's 128 keys: S^T = K Q_h^T and
+//       dP^T = V dO_h^T (N = 64); P^T and dS^T are written back as packed
+//       bf16 over those columns and feed dV += P^T dO_h and dK += dS^T Q_h as
+//       TS-MMAs (A from TMEM, B the streamed tile read MN-major).
+//   Q kernel, TMEM lanes = the CTA's 128 queries: S = Q K_h^T, dP = dO V_h^T;
+//       dS written back feeds dQ += dS K_h.
+// The next block's scores for half h are issued right after half h's
+// gradient MMAs (MMAs from one thread execute in order, so they land after
+// those MMAs have read P / dS). Each compute warp packs its 32 columns into
+// the first 16 of its own 32, so no warp writes columns another still reads.
+// TMEM: dV or dQ [0,128), dK [128,256); half h scores at s_base + 128 h and
+// its dP 64 columns further (s_base 256 for KV, 128 for Q). All waits are
+// bounded (ptx.cuh).
 #include <cuda_bf16.h>
 #include <math.h>
 
@@ -50,8 +54,8 @@ constexpr int kHalf = 16384;
 constexpr int kThreads = 320;
 constexpr int kComputeWarps = 8;  // two per TMEM lane quadrant, one per 64-column half
 constexpr int kModeKV = 0, kModeQ = 1;
-// Resident pair (K,V or Q,dO), a 2-stage ring of streamed pairs, the P/dS tile.
-constexpr int kSmem = 2 * kTile + 2 * 2 * kTile + kTile + 1024 + 256;
+// Resident pair (K,V or Q,dO) and a 2-stage ring of streamed pairs.
+constexpr int kSmem = 2 * kTile + 2 * 2 * kTile + 1024 + 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdParams {
@@ -89,50 +93,46 @@ __device__ __forceinline__ uint64_t mnmajor(uint32_t base, int kk) {
   return sw128_desc(base + kk * 2048, kHalf, 1024);
 }
 
-// Byte offset of the 16-byte group holding columns [c, c + 8) of row r in a
-// swizzled tile (c a multiple of 8).
-__device__ __forceinline__ uint32_t swz_off(int r, int c) {
-  return (uint32_t)((c >> 6) * kHalf + r * 128 + ((((c & 63) >> 3) ^ (r & 7)) << 4));
-}
-
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-
-// Delta[q] = sum_d dO[q, d] O[q, d] in fp32, one warp per query row.
+// Delta[q] = sum_d dO[q, d] O[q, d] in fp32: 16 lanes per query row, one
+// 16-byte load of O and of dO per lane, two rows per warp.
 __global__ void attn_bwd_delta_kernel(int batch, int heads, int seq, const __nv_bfloat16* __restrict__ o,
                                       long long o_sb, long long o_sh, long long o_ss,
                                       const __nv_bfloat16* __restrict__ dout, long long d_sb, long long d_sh,
                                       long long d_ss, float* __restrict__ delta) {
-  const long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+  const long long row = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int part = threadIdx.x & 15;
   const long long rows = (long long)batch * heads * seq;
-  if (row >= rows) return;
-  const int s = (int)(row % seq);
-  const long long bh = row / seq;
-  const int h = (int)(bh % heads), b = (int)(bh / heads);
-  const uint2 ov = *reinterpret_cast<const uint2*>(o + b * o_sb + h * o_sh + s * o_ss + lane * 4);
-  const uint2 dv = *reinterpret_cast<const uint2*>(dout + b * d_sb + h * d_sh + s * d_ss + lane * 4);
-  const __nv_bfloat162* op = reinterpret_cast<const __nv_bfloat162*>(&ov);
-  const __nv_bfloat162* dp = reinterpret_cast<const __nv_bfloat162*>(&dv);
+  const bool live = row < rows;
   float acc = 0.f;
+  if (live) {
+    const int s = (int)(row % seq);
+    const long long bh = row / seq;
+    const int h = (int)(bh % heads), b = (int)(bh / heads);
+    const uint4 ov = __ldcs(reinterpret_cast<const uint4*>(o + b * o_sb + h * o_sh + s * o_ss) + part);
+    const uint4 dv = __ldcs(reinterpret_cast<const uint4*>(dout + b * d_sb + h * d_sh + s * d_ss) + part);
+    const __nv_bfloat162* op = reinterpret_cast<const __nv_bfloat162*>(&ov);
+    const __nv_bfloat162* dp = reinterpret_cast<const __nv_bfloat162*>(&dv);
 #pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const float2 a = __bfloat1622float2(op[e]), c = __bfloat1622float2(dp[e]);
-    acc = fmaf(a.x, c.x, acc);
-    acc = fmaf(a.y, c.y, acc);
+    for (int e = 0; e < 4; ++e) {
+      const float2 a = __bfloat1622float2(op[e]), c = __bfloat1622float2(dp[e]);
+      acc = fmaf(a.x, c.x, acc);
+      acc = fmaf(a.y, c.y, acc);
+    }
   }
 #pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) delta[row] = acc;
+  for (int off = 8; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (live && part == 0) delta[row] = acc;
 }
+
+// TMEM column of the k-th 16-element slice of a half-block operand written by
+// the compute warps: warp sub s of a quadrant packs its 32 columns (16 bf16
+// pairs) at offset 32 s, so slices 0,1 sit at 0, 8 and slices 2,3 at 32, 40.
+__device__ __forceinline__ uint32_t half_col(int kk) { return (uint32_t)((kk >> 1) * 32 + (kk & 1) * 8); }
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -142,21 +142,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
-  uint8_t* sRes = smem;              // KV: K, V.  Q: Q, dO.
+  uint8_t* sRes = smem;               // KV: K, V.  Q: Q, dO.
   uint8_t* sRing = sRes + 2 * kTile;  // stage s: pair at s * 2 * kTile (KV: Q, dO.  Q: K, V)
-  uint8_t* sPS = sRing + 4 * kTile;   // P / dS tile
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sPS + kTile);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + 4 * kTile);
   uint64_t* res_full = bars;
   uint64_t* ring_full = bars + 1;   // [2]
   uint64_t* ring_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;      // S and dP in TMEM
-  uint64_t* p_full = bars + 6;      // KV: P in smem, S/dP read (4 warps)
-  uint64_t* ps_read = bars + 7;     // KV: dV has consumed P
-  uint64_t* ds_full = bars + 8;     // dS in smem (4 warps); Q: also S/dP read
-  uint64_t* ps_free = bars + 9;     // the MMA reading dS has completed
-  uint64_t* acc_done = bars + 10;
-  uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* s_full = bars + 5;      // [2] scores of half h in TMEM
+  uint64_t* p_full = bars + 7;      // [2] half h's P / dS written back to TMEM (8 warps)
+  uint64_t* acc_done = bars + 9;
+  uint64_t* drain = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -169,18 +165,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int bi = bh / p.heads, hi = bh - bi * p.heads;
   const int it0 = (MODE == kModeKV && p.causal) ? own : 0;
   const int n_it = MODE == kModeKV ? p.n_qb - it0 : (p.causal ? min(own + 1, p.n_kb) : p.n_kb);
+  // TMEM: accumulators at 0 (dV or dQ) and 128 (dK); half h's scores at
+  // s_base + 128 h, its dP 64 columns further.
+  constexpr uint32_t s_base = MODE == kModeKV ? 256u : 128u;
 
   if (threadIdx.x == 0) {
     mbar_init(res_full, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&ring_full[s], 1);
       mbar_init(&ring_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], kComputeWarps);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, kComputeWarps);
-    mbar_init(ps_read, 1);
-    mbar_init(ds_full, kComputeWarps);
-    mbar_init(ps_free, 1);
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -239,64 +235,60 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_s = make_idesc(1, 1, 1, 0, 0, 128, 128);   // S, dP: both K-major
-      constexpr uint32_t idesc_kv = make_idesc(1, 1, 1, 1, 1, 128, 128);  // dV, dK: P^T / dS^T and dO / Q MN-major
-      constexpr uint32_t idesc_q = make_idesc(1, 1, 1, 0, 1, 128, 128);   // dQ: dS K-major, K MN-major
-      const uint32_t res = smem_u32(sRes), ring = smem_u32(sRing), ps = smem_u32(sPS);
-      auto q_of = [&](int t) { return MODE == kModeKV ? ring + (t & 1) * 2 * kTile : res; };
-      auto do_of = [&](int t) { return q_of(t) + kTile; };
-      auto k_of = [&](int t) { return MODE == kModeKV ? res : ring + (t & 1) * 2 * kTile; };
-      auto v_of = [&](int t) { return k_of(t) + kTile; };
-      auto scores = [&](int t) {
-        const uint32_t qa = q_of(t), ka = k_of(t), da = do_of(t), va = v_of(t);
+      constexpr uint32_t idesc_s = make_idesc(1, 1, 1, 0, 0, 128, 64);   // scores of a half: N = 64
+      constexpr uint32_t idesc_g = make_idesc(1, 1, 1, 0, 1, 128, 128);  // A from TMEM, B MN-major, N = 128
+      const uint32_t res = smem_u32(sRes), ring = smem_u32(sRing);
+      // Per half h of streamed block t: scores (A resident, K-major; B the
+      // streamed tile's rows [64 h, 64 h + 64), K-major) and dP likewise.
+      auto scores = [&](int t, int h) {
+        const uint32_t st = ring + (t & 1) * 2 * kTile + h * 8192;
+        const uint32_t d_s = tmem + s_base + 128 * h;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) mma_ss<0>(tmem, kmajor(qa, kk), kmajor(ka, kk), idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) mma_ss<0>(d_s, kmajor(res, kk), kmajor(st, kk), idesc_s, kk > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_ss<0>(tmem + 128, kmajor(da, kk), kmajor(va, kk), idesc_s, kk > 0 ? 1u : 0u);
-        mma_commit(s_full);
+          mma_ss<0>(d_s + 64, kmajor(res + kTile, kk), kmajor(st + kTile, kk), idesc_s, kk > 0 ? 1u : 0u);
+        mma_commit(&s_full[h]);
       };
       bool ok = wait_bounded(res_full, 0, wc, kErrTimeoutMma) && wait_bounded(&ring_full[0], 0, wc, kErrTimeoutMma);
       if (ok) {
         tc_fence_after();
-        scores(0);
+        scores(0, 0);
+        scores(0, 1);
       }
       for (int t = 0; t < n_it && ok; ++t) {
-        const bool next = t + 1 < n_it;
-        if (MODE == kModeKV) {
-          if (!wait_bounded(p_full, t & 1, wc, kErrTimeoutMma)) break;
-          tc_fence_after();
-          const uint32_t da = do_of(t);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ss<0>(tmem + 256, mnmajor(ps, kk), mnmajor(da, kk), idesc_kv, (t > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(ps_read);
-          if (next) {
-            if (!wait_bounded(&ring_full[(t + 1) & 1], ((t + 1) >> 1) & 1, wc, kErrTimeoutMma)) break;
-            tc_fence_after();
-            scores(t + 1);
+        const uint32_t st = ring + (t & 1) * 2 * kTile;
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!wait_bounded(&p_full[h], t & 1, wc, kErrTimeoutMma)) {
+            ok = false;
+            break;
           }
-          if (!wait_bounded(ds_full, t & 1, wc, kErrTimeoutMma)) break;
           tc_fence_after();
-          const uint32_t qa = q_of(t);
+          const uint32_t sh = tmem + s_base + 128 * h;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ss<0>(tmem + 384, mnmajor(ps, kk), mnmajor(qa, kk), idesc_kv, (t > 0 || kk > 0) ? 1u : 0u);
-        } else {
-          if (!wait_bounded(ds_full, t & 1, wc, kErrTimeoutMma)) break;
-          tc_fence_after();
-          if (next) {
-            if (!wait_bounded(&ring_full[(t + 1) & 1], ((t + 1) >> 1) & 1, wc, kErrTimeoutMma)) break;
-            tc_fence_after();
-            scores(t + 1);
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t acc = (t > 0 || h > 0 || kk > 0) ? 1u : 0u;
+            if (MODE == kModeKV) {
+              // dV += P^T dO_h, dK += dS^T Q_h (M = keys, K = this half's 64 queries)
+              mma_ts_f16(tmem, sh + half_col(kk), mnmajor(st + kTile + h * 8192, kk), idesc_g, acc);
+              mma_ts_f16(tmem + 128, sh + 64 + half_col(kk), mnmajor(st + h * 8192, kk), idesc_g, acc);
+            } else {
+              // dQ += dS_h K_h (M = queries, K = this half's 64 keys)
+              mma_ts_f16(tmem, sh + half_col(kk), mnmajor(st + h * 8192, kk), idesc_g, acc);
+            }
           }
-          const uint32_t ka = k_of(t);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk)
-            mma_ss<0>(tmem + 256, kmajor(ps, kk), mnmajor(ka, kk), idesc_q, (t > 0 || kk > 0) ? 1u : 0u);
+          if (h == 1) mma_commit(&ring_empty[t & 1]);
+          if (t + 1 < n_it) {
+            // In-order execution: the next scores land after the MMAs above
+            // have read this half's columns.
+            if (h == 0 && !wait_bounded(&ring_full[(t + 1) & 1], ((t + 1) >> 1) & 1, wc, kErrTimeoutMma)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            scores(t + 1, h);
+          }
         }
-        mma_commit(ps_free);
-        mma_commit(&ring_empty[t & 1]);
       }
       mma_commit(acc_done);
       // Every MMA this thread issued must complete before TMEM is released.
@@ -306,93 +298,101 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ P / dS and the epilogue
     const int q = warp & 3;
-    const int cb = ((warp - 2) >> 2) * 64;  // this warp's 64 of the 128 key (or head-dim) columns
+    const int sub = (warp - 2) >> 2;  // which 32 of a half's 64 columns
     const int row = q * 32 + lane;
     const uint32_t t_row = tmem + ((uint32_t)(q * 32) << 16);
-    const uint32_t ps = smem_u32(sPS);
     const long long stat_base = (long long)bh * p.seq_q;
+    // Rows: KV keys of block `own`; Q queries of block `own`.
+    const int rabs = own * kB + row;
+    float row_lse = 0.f, row_dlt = 0.f;
+    if (MODE == kModeQ && rabs < p.seq_q) {
+      row_lse = p.lse[stat_base + rabs] * kLog2e;
+      row_dlt = p.delta[stat_base + rabs];
+    }
     bool ok = true;
     for (int t = 0; t < n_it && ok; ++t) {
-      const int qblk = MODE == kModeKV ? it0 + t : own;
-      const int kblk = MODE == kModeKV ? own : t;
-      const int qabs = qblk * kB + row;
-      const bool qvalid = qabs < p.seq_q;
-      const float lse_l2 = qvalid ? p.lse[stat_base + qabs] * kLog2e : 0.f;
-      const float dlt = qvalid ? p.delta[stat_base + qabs] : 0.f;
-      if (!wait_bounded(s_full, t & 1, wc, kErrTimeoutEpilogue)) break;
-      tc_fence_after();
-      // The P/dS tile still holds the previous block's dS until its MMA ends.
-      if (t > 0 && !wait_bounded(ps_free, (t - 1) & 1, wc, kErrTimeoutEpilogue)) break;
-      uint32_t ds_pk[MODE == kModeKV ? 32 : 1];
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int col = cb + c * 32;
+      const int blk = it0 + t;  // streamed block (KV: query block, Q: key block)
+      for (int h = 0; h < 2; ++h) {
+        const int cbase = blk * kB + h * 64 + sub * 32;  // first column index (query or key)
+        float col_lse = 0.f, col_dlt = 0.f;
+        if (MODE == kModeKV && cbase + lane < p.seq_q) {
+          col_lse = p.lse[stat_base + cbase + lane] * kLog2e;
+          col_dlt = p.delta[stat_base + cbase + lane];
+        }
+        if (!wait_bounded(&s_full[h], t & 1, wc, kErrTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t scol = s_base + 128 * h + 32 * sub;
         uint32_t rs[32], rd[32];
-        tmem_ld_32x32b_x32(t_row + col, rs);
-        tmem_ld_32x32b_x32(t_row + 128 + col, rd);
+        tmem_ld_32x32b_x32(t_row + scol, rs);
+        tmem_ld_32x32b_x32(t_row + scol + 64, rd);
         tmem_ld_wait();
+        // The mask matters only on the causal diagonal and past the sequence
+        // ends; every other (warp, half) block skips the per-element test.
+        const int rlo = own * kB + q * 32, clo = cbase;  // this warp's first row / column
+        bool all_valid;
+        if (MODE == kModeKV)  // rows keys [rlo, rlo + 32), columns queries [clo, clo + 32)
+          all_valid = rlo + 32 <= p.seq_k && clo + 32 <= p.seq_q && (!p.causal || rlo + 31 <= clo);
+        else  // rows queries, columns keys
+          all_valid = rlo + 32 <= p.seq_q && clo + 32 <= p.seq_k && (!p.causal || clo + 31 <= rlo);
         uint32_t pp[16], dd[16];
 #pragma unroll
         for (int jj = 0; jj < 32; jj += 2) {
           float pv[2], dv[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int k = kblk * kB + col + jj + e;
-            const bool valid = qvalid && k < p.seq_k && (!p.causal || k <= qabs);
+            const int c = cbase + jj + e;
+            float lse_l2, dlt;
+            bool valid = true;
+            if (MODE == kModeKV) {  // row = key rabs, column = query c
+              lse_l2 = __shfl_sync(0xffffffffu, col_lse, jj + e);
+              dlt = __shfl_sync(0xffffffffu, col_dlt, jj + e);
+              if (!all_valid) valid = c < p.seq_q && rabs < p.seq_k && (!p.causal || rabs <= c);
+            } else {  // row = query rabs, column = key c
+              lse_l2 = row_lse;
+              dlt = row_dlt;
+              if (!all_valid) valid = rabs < p.seq_q && c < p.seq_k && (!p.causal || c <= rabs);
+            }
             pv[e] = valid ? ex2_approx(fmaf(__uint_as_float(rs[jj + e]), p.scale_log2, -lse_l2)) : 0.f;
             dv[e] = pv[e] * (__uint_as_float(rd[jj + e]) - dlt);
           }
           pp[jj / 2] = pack_bf16(pv[0], pv[1]);
           dd[jj / 2] = pack_bf16(dv[0], dv[1]);
         }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          if (MODE == kModeKV) {
-            st_shared_v4(ps + swz_off(row, col + g * 8), pp[4 * g], pp[4 * g + 1], pp[4 * g + 2], pp[4 * g + 3]);
-#pragma unroll
-            for (int e = 0; e < 4; ++e) ds_pk[c * 16 + 4 * g + e] = dd[4 * g + e];
-          } else {
-            st_shared_v4(ps + swz_off(row, col + g * 8), dd[4 * g], dd[4 * g + 1], dd[4 * g + 2], dd[4 * g + 3]);
-          }
+        // This warp's 32 columns, packed, over its own scores (P) and dP (dS).
+        if (MODE == kModeKV) {
+          tmem_st_32x32b_x16(t_row + scol, pp);
+          tmem_st_32x32b_x16(t_row + scol + 64, dd);
+        } else {
+          tmem_st_32x32b_x16(t_row + scol, dd);
         }
-      }
-      tc_fence_before();
-      fence_async_smem();
-      __syncwarp();
-      if (MODE == kModeKV) {
-        if (lane == 0) mbar_arrive(p_full);
-        // dS replaces P once dV has read it.
-        if (!wait_bounded(ps_read, t & 1, wc, kErrTimeoutEpilogue)) break;
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int g = 0; g < 4; ++g)
-            st_shared_v4(ps + swz_off(row, cb + c * 32 + g * 8), ds_pk[c * 16 + 4 * g], ds_pk[c * 16 + 4 * g + 1],
-                         ds_pk[c * 16 + 4 * g + 2], ds_pk[c * 16 + 4 * g + 3]);
-        fence_async_smem();
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[h]);
       }
-      if (lane == 0) mbar_arrive(ds_full);
     }
     if (ok && wait_bounded(acc_done, 0, wc, kErrTimeoutEpilogue) && !*abort_flag) {
       tc_fence_after();
-      // KV: dK (scaled) from [384, 512) to out0, dV from [256, 384) to out1.
-      // Q: dQ (scaled) from [256, 384) to out0.
-      const int rabs = own * kB + row;
+      // KV: dK (scaled) from [128, 256) to out0, dV from [0, 128) to out1.
+      // Q: dQ (scaled) from [0, 128) to out0. Warp sub writes columns [64 sub, +64).
       const bool rvalid = rabs < (MODE == kModeKV ? p.seq_k : p.seq_q);
       for (int which = 0; which < (MODE == kModeKV ? 2 : 1); ++which) {
-        const uint32_t col = MODE == kModeKV ? (which == 0 ? 384u : 256u) : 256u;
+        const uint32_t col = MODE == kModeKV ? (which == 0 ? 128u : 0u) : 0u;
         const float mul = which == 0 ? p.scale : 1.f;
         __nv_bfloat16* out = static_cast<__nv_bfloat16*>(which == 0 ? p.out0 : p.out1) +
                              (which == 0 ? (long long)bi * p.o0_sb + (long long)hi * p.o0_sh + (long long)rabs * p.o0_ss
                                          : (long long)bi * p.o1_sb + (long long)hi * p.o1_sh + (long long)rabs * p.o1_ss);
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
+          const int c0 = sub * 64 + c * 32;
           uint32_t v[32];
-          tmem_ld_32x32b_x32(t_row + col + cb + c * 32, v);
+          tmem_ld_32x32b_x32(t_row + col + c0, v);
           tmem_ld_wait();
           if (rvalid) {
-            uint4* dst = reinterpret_cast<uint4*>(out + cb + c * 32);
+            uint4* dst = reinterpret_cast<uint4*>(out + c0);
 #pragma unroll
             for (int g = 0; g < 4; ++g) {
               uint32_t w[4];
@@ -488,11 +488,13 @@ cudaError_t launch_attention_bwd(const AttnBwdArgs& a, void* ws, size_t ws_bytes
   const long long oss[3] = {a.dq_ss, a.dk_ss, a.dv_ss};
   for (int i = 0; i < 3; ++i)
     if ((reinterpret_cast<uintptr_t>(outs[i]) & 15u) || (oss[i] * 2) % 16) return cudaErrorNotSupported;
-  if ((reinterpret_cast<uintptr_t>(a.o) & 7u) || (reinterpret_cast<uintptr_t>(a.dout) & 7u)) return cudaErrorNotSupported;
+  if ((reinterpret_cast<uintptr_t>(a.o) & 15u) || (reinterpret_cast<uintptr_t>(a.dout) & 15u) || (a.o_ss * 2) % 16 ||
+      (a.do_ss * 2) % 16 || (a.o_sh * 2) % 16 || (a.o_sb * 2) % 16 || (a.do_sh * 2) % 16 || (a.do_sb * 2) % 16)
+    return cudaErrorNotSupported;
   float* delta = static_cast<float*>(ws);
   {
     const long long rows = (long long)a.batch * a.heads * a.seq_q;
-    const long long blocks = (rows + 7) / 8;
+    const long long blocks = (rows + 15) / 16;  // 256 threads = 16 rows
     if (blocks > 0x7fffffffLL) return cudaErrorInvalidValue;
     ProfLaunch prof("attn_bwd_delta_kernel", dim3((unsigned)blocks), dim3(256), 0, s);
     attn_bwd_delta_kernel<<<(unsigned)blocks, 256, 0, s>>>(
