@@ -129,6 +129,31 @@ __global__ void attn_bwd_delta_kernel(int batch, int heads, int seq, const __nv_
   if (live && part == 0) delta[row] = acc;
 }
 
+// Packed fp32 pairs (sm_100 executes f32x2 FMA / ADD / MUL as one instruction).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // TMEM column of the k-th 16-element slice of a half-block operand written by
 // the compute warps: warp sub s of a quadrant packs its 32 columns (16 bf16
 // pairs) at offset 32 s, so slices 0,1 sit at 0, 8 and slices 2,3 at 32, 40.
@@ -154,6 +179,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* drain = bars + 10;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // KV kernel: per compute warp, its 32 columns' (-LSE log2 e, Delta) pairs.
+  __shared__ __align__(16) float2 col_stats[kComputeWarps][32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_own = MODE == kModeKV ? p.n_kb : p.n_qb;
@@ -319,6 +346,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           col_lse = p.lse[stat_base + cbase + lane] * kLog2e;
           col_dlt = p.delta[stat_base + cbase + lane];
         }
+        if (MODE == kModeKV) {
+          __syncwarp();  // the previous half's reads of the slot are done
+          col_stats[warp - 2][lane] = make_float2(-col_lse, col_dlt);
+          __syncwarp();
+        }
         if (!wait_bounded(&s_full[h], t & 1, wc, kErrTimeoutEpilogue)) {
           ok = false;
           break;
@@ -338,6 +370,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         else  // rows queries, columns keys
           all_valid = rlo + 32 <= p.seq_q && clo + 32 <= p.seq_k && (!p.causal || clo + 31 <= rlo);
         uint32_t pp[16], dd[16];
+        if (all_valid) {
+          // Packed pairs: x = S scale log2e - LSE log2e, P = 2^x, dS = P (dP - Delta).
+          const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+          const uint64_t nl_row = f2_pack(-row_lse, -row_lse), nd_row = f2_pack(-row_dlt, -row_dlt);
+          const float4* st4 = reinterpret_cast<const float4*>(col_stats[warp - 2]);
+#pragma unroll
+          for (int jj = 0; jj < 32; jj += 2) {
+            uint64_t nl2, nd2;
+            if (MODE == kModeKV) {
+              const float4 cs = st4[jj / 2];  // (-lse, dlt) of columns jj, jj + 1 (a broadcast load)
+              nl2 = f2_pack(cs.x, cs.z);
+              nd2 = f2_pack(-cs.y, -cs.w);
+            } else {
+              nl2 = nl_row;
+              nd2 = nd_row;
+            }
+            const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(rs[jj]), __uint_as_float(rs[jj + 1])), sc2, nl2);
+            float x0, x1;
+            f2_unpack(x2, x0, x1);
+            const uint64_t p2 = f2_pack(ex2_approx(x0), ex2_approx(x1));
+            const uint64_t d2 =
+                f2_mul(p2, f2_add(f2_pack(__uint_as_float(rd[jj]), __uint_as_float(rd[jj + 1])), nd2));
+            float p0, p1, d0, d1;
+            f2_unpack(p2, p0, p1);
+            f2_unpack(d2, d0, d1);
+            pp[jj / 2] = pack_bf16(p0, p1);
+            dd[jj / 2] = pack_bf16(d0, d1);
+          }
+        } else
 #pragma unroll
         for (int jj = 0; jj < 32; jj += 2) {
           float pv[2], dv[2];
