@@ -40,6 +40,7 @@
 #include <mutex>
 
 #include "attention.cuh"
+#include "exp2_poly.cuh"
 #include "profile.h"
 #include "ptx.cuh"
 
@@ -57,6 +58,9 @@ constexpr int kModeKV = 0, kModeQ = 1;
 // Resident pair (K,V or Q,dO) and a 2-stage ring of streamed pairs.
 constexpr int kSmem = 2 * kTile + 2 * 2 * kTile + 1024 + 256;
 constexpr float kLog2e = 1.4426950408889634f;
+// Share of exponentials moved to the FMA pipe (every n-th pair; 0 = none). Measured at config 4:
+// none 4.66 ms, 1/8 4.80, 1/4 4.93, 1/2 5.11 -- this stage is FMA-issue bound, not SFU bound.
+constexpr int kPolyEveryBwd = 0;
 
 struct BwdParams {
   int batch, heads, seq_q, seq_k, n_qb, n_kb, causal;
@@ -389,7 +393,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(rs[jj]), __uint_as_float(rs[jj + 1])), sc2, nl2);
             float x0, x1;
             f2_unpack(x2, x0, x1);
-            const uint64_t p2 = f2_pack(ex2_approx(x0), ex2_approx(x1));
+            // Every kPolyEveryBwd-th pair on the FMA pipe, the rest on the SFU.
+            const bool poly = kPolyEveryBwd > 0 && (jj / 2) % kPolyEveryBwd == kPolyEveryBwd - 1;
+            const uint64_t p2 = poly ? f2_pack(exp2_poly(x0), exp2_poly(x1)) : f2_pack(ex2_approx(x0), ex2_approx(x1));
             const uint64_t d2 =
                 f2_mul(p2, f2_add(f2_pack(__uint_as_float(rd[jj]), __uint_as_float(rd[jj + 1])), nd2));
             float p0, p1, d0, d1;
