@@ -49,6 +49,10 @@ class grxblasEpilogue_t(C.Structure):
     ]
 
 
+class grxIpcMemHandle_t(C.Structure):
+    _fields_ = [("reserved", C.c_ubyte * 64)]
+
+
 class grxdnnConvDesc_t(C.Structure):
     _fields_ = [(f, i32) for f in ("n", "h", "w", "c", "k", "r", "s", "padH", "padW", "strideH", "strideW",
                                    "dilationH", "dilationW")]
@@ -202,6 +206,10 @@ PROTOTYPES: dict[str, tuple] = {
             vp,
         ],
     ),
+    "grxblasSetPeerOutputs": (i32, [vp, i32, vp]),
+    "grxIpcGetMemHandle": (i32, [vp, vp]),
+    "grxIpcOpenMemHandle": (i32, [vp, grxIpcMemHandle_t]),
+    "grxIpcCloseMemHandle": (i32, [vp]),
     "grxdnnConvOutputDims": (i32, [vp, vp, vp]),
     "grxdnnConv2dForward": (i32, [vp, vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32]),
     "grxdnnPoolingOutputDims": (i32, [vp, vp, vp]),

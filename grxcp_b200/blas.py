@@ -117,6 +117,11 @@ class Handle:
     def clear_epilogue(self) -> int:
         return lib.grxblasSetEpilogue(self.h, None)
 
+    def set_peer_outputs(self, peers) -> int:
+        """grxblasSetPeerOutputs: device addresses (ints) of peer copies of C; [] clears."""
+        arr = (C.c_void_p * max(1, len(peers)))(*[C.c_void_p(int(x)) for x in peers])
+        return lib.grxblasSetPeerOutputs(self.h, len(peers), arr if peers else None)
+
     def set_workspace(self, ws, nbytes: int) -> int:
         return lib.grxblasSetWorkspace(self.h, ptr(ws), nbytes)
 

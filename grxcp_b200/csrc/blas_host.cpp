@@ -36,6 +36,8 @@ struct grxblasContext {
   size_t ws_own_bytes = 0;
   grx::DeviceState dev;
   bool loaded = false;
+  int n_peers = 0;
+  void* peers[grx::kMaxPeers] = {};
 };
 
 namespace {
@@ -222,6 +224,7 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
   if (tc.out == grx::kOutS32 && ctx.has_epi && (epi.activation != GRXBLAS_ACT_NONE)) return GRXBLAS_STATUS_NOT_SUPPORTED;
   const int bias_bf16 = (epi.bias && epi.biasType == GRX_R_16BF) ? 1 : 0;
 
+  if (ctx.n_peers > 0 && (k == 0 || tc.kind != grx::kKindF16)) return GRXBLAS_STATUS_NOT_SUPPORTED;
   if (k == 0) {
     // C = beta*C (+ bias): no product to form (reference test case "k = 0
     // scales C by beta", tests/libs/test_grxblas_ex.cpp:217).
@@ -303,6 +306,8 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
   p.err_word = ctx.dev.err_word;
   p.timeout_ns = grx::wait_timeout_ns();
   p.group_m = 16;
+  p.n_peers = ctx.n_peers;
+  for (int i = 0; i < ctx.n_peers; ++i) p.peers[i] = ctx.peers[i];
   return from_cuda(grx::launch_tc_gemm(L, ctx.dev.num_sms, ctx.stream));
 }
 
@@ -410,6 +415,18 @@ grxblasStatus_t grxblasGemmStridedBatchedEx(grxblasHandle_t handle, grxblasOpera
                                             long long strideC, int batchCount) {
   return gemm_ex_impl(handle, transa, transb, m, n, k, alpha, A, Atype, lda, strideA, B, Btype, ldb, strideB, beta,
                       C, Ctype, ldc, strideC, batchCount);
+}
+
+grxblasStatus_t grxblasSetPeerOutputs(grxblasHandle_t handle, int n, void* const* peers) {
+  if (!handle) return GRXBLAS_STATUS_NOT_INITIALIZED;
+  if (n < 0 || n > grx::kMaxPeers || (n > 0 && !peers)) return GRXBLAS_STATUS_INVALID_VALUE;
+  for (int i = 0; i < n; ++i)
+    if (!peers[i]) return GRXBLAS_STATUS_INVALID_VALUE;
+  auto* ctx = reinterpret_cast<grxblasContext*>(handle);
+  std::lock_guard<std::mutex> lock(ctx->mutex);
+  ctx->n_peers = peers ? n : 0;
+  for (int i = 0; i < grx::kMaxPeers; ++i) ctx->peers[i] = i < ctx->n_peers ? peers[i] : nullptr;
+  return GRXBLAS_STATUS_SUCCESS;
 }
 
 grxblasStatus_t grxblasSetEpilogue(grxblasHandle_t handle, const grxblasEpilogue_t* epilogue) {

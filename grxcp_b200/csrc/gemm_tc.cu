@@ -253,7 +253,9 @@ struct EpiRow {
 // ncol: how many of the chunk's 32 columns exist (the rest are not stored).
 // MASKED: the pair-store path takes partial chunks too (conv); otherwise it
 // takes full chunks only and partial ones go element by element (GEMM).
-template <int KIND, int OUT, bool MASKED = false>
+// PEER: every value stored to C is stored at the same offset in each of the
+// p.n_peers peer buffers too (plain stores over NVLink into other GPUs' C).
+template <int KIND, int OUT, bool MASKED = false, bool PEER = false>
 __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& er, uint32_t (&r)[32], int jbase,
                                           int ncol, float sb_l, float bias_l, const float* sb, const float* bias_f,
                                           const __nv_bfloat16* bias_h) {
@@ -305,11 +307,21 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& e
         const long long off = base + (long long)(jj / 2) * step;
         if (MASKED && jj + (odd ? 1 : 0) >= ncol) continue;
         if constexpr (OUT == kOutF32) {
-          *reinterpret_cast<float2*>(static_cast<float*>(p.c) + off) = make_float2(lo, hi);
+          const float2 w = make_float2(lo, hi);
+          *reinterpret_cast<float2*>(static_cast<float*>(p.c) + off) = w;
+          if constexpr (PEER)
+            for (int pr = 0; pr < p.n_peers; ++pr) *reinterpret_cast<float2*>(static_cast<float*>(p.peers[pr]) + off) = w;
         } else if constexpr (OUT == kOutBF16) {
-          *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.c) + off) = __floats2bfloat162_rn(lo, hi);
+          const __nv_bfloat162 w = __floats2bfloat162_rn(lo, hi);
+          *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.c) + off) = w;
+          if constexpr (PEER)
+            for (int pr = 0; pr < p.n_peers; ++pr)
+              *reinterpret_cast<__nv_bfloat162*>(static_cast<__nv_bfloat16*>(p.peers[pr]) + off) = w;
         } else {
-          *reinterpret_cast<__half2*>(static_cast<__half*>(p.c) + off) = __floats2half2_rn(lo, hi);
+          const __half2 w = __floats2half2_rn(lo, hi);
+          *reinterpret_cast<__half2*>(static_cast<__half*>(p.c) + off) = w;
+          if constexpr (PEER)
+            for (int pr = 0; pr < p.n_peers; ++pr) *reinterpret_cast<__half2*>(static_cast<__half*>(p.peers[pr]) + off) = w;
         }
       }
     }
@@ -328,7 +340,10 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& e
       } else {
         float v = epi_scaled<KIND>(p, r[jj], er.rowmul, sb, j);
         if (p.beta_nonzero) v = __fadd_rn(v, __fmul_rn(p.beta, load_c<OUT>(p.c, idx)));
-        store_c<OUT>(p.c, idx, epi_bias(p, v, bias_f, bias_h, j, er.bias_row));
+        v = epi_bias(p, v, bias_f, bias_h, j, er.bias_row);
+        store_c<OUT>(p.c, idx, v);
+        if constexpr (PEER)
+          for (int pr = 0; pr < p.n_peers; ++pr) store_c<OUT>(p.peers[pr], idx, v);
       }
     }
   }
@@ -336,7 +351,7 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& e
 
 constexpr int kEpiChunks = kTileN / 2 / 32;  // chunks of one epilogue warp's column half
 
-template <int KIND, int OUT>
+template <int KIND, int OUT, bool PEER = false>
 __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_row, int bt, int i, int col0, int cb) {
   constexpr int kOutBytes = (OUT == kOutBF16 || OUT == kOutF16) ? 2 : 4;
   const int lane = threadIdx.x & 31;
@@ -376,12 +391,12 @@ __device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_
     if (ci >= nch) break;
     tmem_ld_wait_regs(ra);
     if (ci + 1 < nch) tmem_ld_32x32b_x32(t_row + cb + (ci + 1) * 32, rb);
-    epi_chunk<KIND, OUT>(p, er, ra, col0 + cb + ci * 32, min(32, p.n - (col0 + cb + ci * 32)), sb_pre[ci],
+    epi_chunk<KIND, OUT, false, PEER>(p, er, ra, col0 + cb + ci * 32, min(32, p.n - (col0 + cb + ci * 32)), sb_pre[ci],
                          bias_pre[ci], sb, bias_f, bias_h);
     if (ci + 1 < nch) {
       tmem_ld_wait_regs(rb);
       if (ci + 2 < nch) tmem_ld_32x32b_x32(t_row + cb + (ci + 2) * 32, ra);
-      epi_chunk<KIND, OUT>(p, er, rb, col0 + cb + (ci + 1) * 32, min(32, p.n - (col0 + cb + (ci + 1) * 32)),
+      epi_chunk<KIND, OUT, false, PEER>(p, er, rb, col0 + cb + (ci + 1) * 32, min(32, p.n - (col0 + cb + (ci + 1) * 32)),
                            sb_pre[ci + 1], bias_pre[ci + 1], sb, bias_f, bias_h);
     }
   }
@@ -428,7 +443,7 @@ __device__ __forceinline__ void epilogue_conv(const TcGemmParams& p, uint32_t t_
   }
 }
 
-template <int KIND, int OUT, bool CONV>
+template <int KIND, int OUT, bool CONV, bool PEER>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ TcGemmParams p) {
@@ -609,7 +624,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if constexpr (CONV) {
         epilogue_conv<KIND, OUT>(p, t_row, mt * kTileM + row, nt, cb);
       } else if (split < 0) {
-        epilogue_tile<KIND, OUT>(p, t_row, bt, mt * kTileM + row, nt * kTileN, cb);
+        epilogue_tile<KIND, OUT, PEER>(p, t_row, bt, mt * kTileM + row, nt * kTileN, cb);
       } else {
         // A cut tile: publish this unit's partial, count it in, and let the
         // last split of the tile to arrive reduce and write C. Nobody waits on
@@ -643,13 +658,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (before == mg.n - 1) {
           __threadfence();
           sk_reduce_into_tmem<KIND>(p, t_row, mg, nt * kTileN, cb, cb + kTileN / 2);
-          epilogue_tile<KIND, OUT>(p, t_row, bt, mt * kTileM + row, nt * kTileN, cb);
+          epilogue_tile<KIND, OUT, PEER>(p, t_row, bt, mt * kTileM + row, nt * kTileN, cb);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[b]);
     }
+    if constexpr (PEER) __threadfence_system();  // this thread's stores into peer GPUs' C are performed
   }
 
   __syncthreads();
@@ -672,7 +688,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 //               TMEM, then one arrival on the leader's accumulator-free barrier.
 // Per SM this halves the B bytes per FLOP of the single-CTA kernel, so the
 // same shared memory keeps the tensor pipe fed across longer L2 latency.
-template <int KIND, int OUT>
+template <int KIND, int OUT, bool PEER>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ TcGemmParams p) {
@@ -838,7 +854,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       int bt, mt, nt;
       decode_tile(p, t, bt, mt, nt);
-      epilogue_tile<KIND, OUT>(p, tmem_base + ((uint32_t)(q * 32) << 16) + b * kPairTileN, bt,
+      epilogue_tile<KIND, OUT, PEER>(p, tmem_base + ((uint32_t)(q * 32) << 16) + b * kPairTileN, bt,
                                mt * kPairTileM + (int)rank * 128 + row, nt * kPairTileN, cb);
       tc_fence_before();
       __syncwarp();
@@ -847,6 +863,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         else mbar_arrive_cluster(&tempty[b], 0);
       }
     }
+    if constexpr (PEER) __threadfence_system();  // this thread's stores into peer GPUs' C are performed
   }
 
   __syncthreads();
@@ -918,10 +935,10 @@ static bool make_operand_map(CUtensorMap* map, const void* base, int es, int mn_
   return r == CUDA_SUCCESS;
 }
 
-template <int KIND, int OUT, bool CONV = false>
+template <int KIND, int OUT, bool CONV = false, bool PEER = false>
 static cudaError_t launch_impl(const CUtensorMap& ma, const CUtensorMap& mb, const TcGemmParams& p, int grid,
                                cudaStream_t s) {
-  auto kfn = tc_gemm_kernel<KIND, OUT, CONV>;
+  auto kfn = tc_gemm_kernel<KIND, OUT, CONV, PEER>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -933,10 +950,10 @@ static cudaError_t launch_impl(const CUtensorMap& ma, const CUtensorMap& mb, con
   return cudaGetLastError();
 }
 
-template <int KIND, int OUT>
+template <int KIND, int OUT, bool PEER = false>
 static cudaError_t launch_pair_impl(const CUtensorMap& ma, const CUtensorMap& mb, const TcGemmParams& p, int grid,
                                     cudaStream_t s) {
-  auto kfn = tc_gemm_pair_kernel<KIND, OUT>;
+  auto kfn = tc_gemm_pair_kernel<KIND, OUT, PEER>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [&] {
@@ -1152,9 +1169,21 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
     return cudaErrorInvalidValue;
   const long long tiles = (long long)p.m_tiles * p.n_tiles * p.batch;
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
+  if (p.n_peers > 0) {
+    // Replicated output: the 16-bit kinds only (the shard layer's bf16 / fp16 path).
+    if (L.kind != kKindF16 || L.out == kOutS32) return cudaErrorNotSupported;
+  }
   if (pair) {
     const int pairs = (int)(tiles < num_sms / 2 ? tiles : num_sms / 2);
     const int g2 = 2 * pairs;
+    if (p.n_peers > 0) {
+      switch (L.out) {
+        case kOutF32: return launch_pair_impl<kKindF16, kOutF32, true>(ma, mb, p, g2, stream);
+        case kOutBF16: return launch_pair_impl<kKindF16, kOutBF16, true>(ma, mb, p, g2, stream);
+        case kOutF16: return launch_pair_impl<kKindF16, kOutF16, true>(ma, mb, p, g2, stream);
+        default: return cudaErrorNotSupported;
+      }
+    }
     switch (L.kind * 4 + L.out) {
       case kKindF16 * 4 + kOutF32: return launch_pair_impl<kKindF16, kOutF32>(ma, mb, p, g2, stream);
       case kKindF16 * 4 + kOutBF16: return launch_pair_impl<kKindF16, kOutBF16>(ma, mb, p, g2, stream);
@@ -1183,6 +1212,14 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
     if (e != cudaSuccess) return e;
     const long long units = sp.dp_tiles + sp.sk_tiles * sp.splits;
     grid = (int)(units < num_sms ? units : num_sms);
+  }
+  if (p.n_peers > 0) {
+    switch (L.out) {
+      case kOutF32: return launch_impl<kKindF16, kOutF32, false, true>(ma, mb, p, grid, stream);
+      case kOutBF16: return launch_impl<kKindF16, kOutBF16, false, true>(ma, mb, p, grid, stream);
+      case kOutF16: return launch_impl<kKindF16, kOutF16, false, true>(ma, mb, p, grid, stream);
+      default: return cudaErrorNotSupported;
+    }
   }
   switch (L.kind * 4 + L.out) {
     case kKindF16 * 4 + kOutF32: return launch_impl<kKindF16, kOutF32>(ma, mb, p, grid, stream);

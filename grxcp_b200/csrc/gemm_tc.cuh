@@ -11,7 +11,8 @@ namespace grx {
 // The kernel refuses to run on a version mismatch (the reference's kernel ABI
 // blocks do the same, src/libs/grxblas/hgemm_abi.h:20 and
 // src/libs/grxblas/kernels/sgemm.cpp:23-27).
-constexpr uint32_t kTcGemmAbi = 5;
+constexpr uint32_t kTcGemmAbi = 6;
+constexpr int kMaxPeers = 7;  // one process per GPU, eight GPUs per node
 
 enum TcKind : int { kKindF16 = 0, kKindI8 = 1, kKindF8 = 2 };
 enum TcOut : int { kOutF32 = 0, kOutBF16 = 1, kOutF16 = 2, kOutS32 = 3 };
@@ -60,6 +61,10 @@ struct TcGemmParams {
   int cv_p, cv_q, cv_th, cv_tw, cv_tiles_p, cv_tiles_q;
   int cv_sh, cv_sw, cv_ph, cv_pw, cv_dh, cv_dw, cv_s, cv_cb;
   uint32_t cv_b_bytes;  // bytes one pixel-block box delivers (th * tw * 128)
+  // Replicated output: every element stored to c is also stored at the same
+  // offset in peers[0 .. n_peers) (other GPUs' buffers opened in this process).
+  int n_peers;
+  void* peers[kMaxPeers];
 };
 
 struct TcGemmLaunch {

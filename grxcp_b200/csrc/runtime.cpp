@@ -193,6 +193,24 @@ grxError_t grxDeviceEnablePeerAccess(int peer, unsigned int flags) {
   return rec(e);
 }
 
+grxError_t grxIpcGetMemHandle(grxIpcMemHandle_t* handle, void* dev_ptr) {
+  static_assert(sizeof(grxIpcMemHandle_t) == sizeof(cudaIpcMemHandle_t), "IPC handle size");
+  if (!handle || !dev_ptr) return rec(cudaErrorInvalidValue);
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, dev_ptr);
+  if (e == cudaSuccess) memcpy(handle, &h, sizeof(h));
+  return rec(e);
+}
+
+grxError_t grxIpcOpenMemHandle(void** dev_ptr, grxIpcMemHandle_t handle) {
+  if (!dev_ptr) return rec(cudaErrorInvalidValue);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, &handle, sizeof(h));
+  return rec(cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+grxError_t grxIpcCloseMemHandle(void* dev_ptr) { return rec(cudaIpcCloseMemHandle(dev_ptr)); }
+
 grxError_t grxGetLastError(void) {
   const grxError_t e = g_last_error;
   g_last_error = grxSuccess;

@@ -86,6 +86,113 @@ def gemm_ex_column_parallel(handle, transa, transb, m, n, k, alpha, A, Atype, ld
     return st
 
 
+class _CudaArray:
+    """A raw device range as a torch-importable object (CUDA array interface)."""
+
+    def __init__(self, ptr: int, numel: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (numel,), "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerBuffer:
+    """One device buffer per rank, each opened in every rank's process.
+
+    The buffer is a grxMalloc allocation (a whole allocation, as CUDA IPC
+    requires); its IPC handle is exchanged through the process group and every
+    peer's copy is opened with grxIpcOpenMemHandle. `ptrs[r]` is rank r's copy
+    as a device address valid in this process; `local(dtype)` is this rank's
+    copy as a flat torch tensor. Collective: every rank constructs it with the
+    same size."""
+
+    def __init__(self, nbytes: int, rank: int, world: int, group=None):
+        import ctypes as C
+
+        import torch.distributed as dist
+
+        self.rank, self.world, self.nbytes = rank, world, nbytes
+        p = C.c_void_p()
+        st = N.lib.grxMalloc(C.byref(p), nbytes)
+        if st != 0 or not p.value:
+            raise RuntimeError(f"grxMalloc({nbytes}) failed: {st}")
+        self._own = p.value
+        h = N.grxIpcMemHandle_t()
+        st = N.lib.grxIpcGetMemHandle(C.byref(h), C.c_void_p(self._own))
+        if st != 0:
+            raise RuntimeError(f"grxIpcGetMemHandle failed: {st}")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(h.reserved), group=group)
+        self.ptrs = []
+        self._opened = []
+        for r in range(world):
+            if r == rank:
+                self.ptrs.append(self._own)
+                continue
+            hr = N.grxIpcMemHandle_t()
+            C.memmove(hr.reserved, handles[r], 64)
+            q = C.c_void_p()
+            st = N.lib.grxIpcOpenMemHandle(C.byref(q), hr)
+            if st != 0 or not q.value:
+                raise RuntimeError(f"grxIpcOpenMemHandle(rank {r}) failed: {st}")
+            self.ptrs.append(q.value)
+            self._opened.append(q.value)
+
+    def local(self, dtype):
+        """This rank's copy as a flat torch tensor of `dtype` (bf16, fp16 or fp32)."""
+        import torch
+
+        es = torch.tensor([], dtype=dtype).element_size()
+        code = {4: "<f4", 2: "<i2"}[es]
+        t = torch.as_tensor(_CudaArray(self._own, self.nbytes // es, code), device="cuda")
+        return t.view(dtype)
+
+    def close(self) -> None:
+        for q in self._opened:
+            N.lib.grxIpcCloseMemHandle(q)
+        self._opened = []
+        if self._own:
+            N.lib.grxFree(self._own)
+            self._own = 0
+
+
+def gemm_ex_column_parallel_fused(handle, transa, transb, m, n, k, alpha, A, Atype, lda, B, Btype, ldb, beta,
+                                  cbuf: PeerBuffer, Ctype, ldc, bias=None, rank: int = 0, world: int = 1,
+                                  group=None) -> int:
+    """Column-parallel GemmEx whose epilogue writes this rank's columns into
+    every rank's copy of C (cbuf, a PeerBuffer holding the full ldc x n C):
+    the replicated-output step fused into the GEMM over NVLink instead of a
+    separate all-gather. Ends with a barrier, after which C is complete on
+    every rank. 16-bit inputs only (grxblasSetPeerOutputs)."""
+    import torch
+    import torch.distributed as dist
+
+    cols = even_shard(n, world, rank)
+    es = 4 if Ctype == N.GRX_R_32F else 2
+    C = cbuf.local(torch.float32 if es == 4 else (torch.bfloat16 if Ctype == N.GRX_R_16BF else torch.float16))
+    b, c, bv = column_views(B, C, bias, transb, ldb, ldc, cols)
+    off = cols.start * ldc * es
+    st = handle.set_peer_outputs([cbuf.ptrs[r] + off for r in range(world) if r != rank])
+    if st != N.SUCCESS:
+        return st
+    if bias is not None:
+        st = handle.set_epilogue(bias=bv, bias_type=N.GRX_R_32F if bias.dtype.itemsize == 4 else N.GRX_R_16BF)
+        if st != N.SUCCESS:
+            return st
+    try:
+        if cols.count > 0:
+            st = handle.gemm_ex(transa, transb, m, cols.count, k, alpha, A, Atype, lda, b, Btype, ldb, beta, c, Ctype,
+                                ldc)
+    finally:
+        handle.set_peer_outputs([])
+        if bias is not None:
+            handle.clear_epilogue()
+    if st == N.SUCCESS and world > 1:
+        # Every rank's kernel (and its stores into the other copies) precedes
+        # its part of this collective on the same stream.
+        dist.barrier(group=group)
+        torch.cuda.synchronize()
+    return st
+
+
 def all_gather_chunks(flat, chunk: int, rank: int, world: int, group=None) -> None:
     """flat holds `world` equal contiguous chunks; chunk `rank` is this rank's.
     After the call every rank holds all of them (NCCL on CUDA tensors, the list

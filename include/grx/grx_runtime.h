@@ -29,6 +29,18 @@ grxError_t grxMemGetInfo(size_t* freeBytes, size_t* totalBytes);
 grxError_t grxDeviceCanAccessPeer(int* canAccess, int device, int peer);
 grxError_t grxDeviceEnablePeerAccess(int peerDevice, unsigned int flags);
 
+/* Inter-process device memory (no counterpart in the reference): export a
+ * handle to a grxMalloc allocation, open a peer process's handle as a device
+ * pointer of this process (peer access enabled lazily), close it. One process
+ * per GPU uses these to let kernels store straight into a peer's buffer over
+ * NVLink (grxblasSetPeerOutputs). devPtr must be the base of an allocation. */
+typedef struct {
+  unsigned char reserved[64];
+} grxIpcMemHandle_t;
+grxError_t grxIpcGetMemHandle(grxIpcMemHandle_t* handle, void* devPtr);
+grxError_t grxIpcOpenMemHandle(void** devPtr, grxIpcMemHandle_t handle);
+grxError_t grxIpcCloseMemHandle(void* devPtr);
+
 /* Sticky last error -- reference grx_runtime.h:44-45 */
 grxError_t grxGetLastError(void);
 grxError_t grxPeekAtLastError(void);

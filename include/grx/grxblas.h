@@ -145,6 +145,19 @@ typedef struct {
 
 grxblasStatus_t grxblasSetEpilogue(grxblasHandle_t handle, const grxblasEpilogue_t* epilogue);
 
+/* Replicated output (no counterpart in the reference, which has no
+ * multi-device path). After this call, every element a 16-bit GemmEx /
+ * GemmStridedBatchedEx on this handle stores to C is also stored at the same
+ * element offset in each of the n peer buffers -- other GPUs' copies of C,
+ * opened in this process with grxIpcOpenMemHandle -- from the same kernel's
+ * epilogue, over NVLink. With one process per GPU each computing its own
+ * columns of C, this assembles C on every GPU in the GEMM itself, without a
+ * separate all-gather. The caller must order the peers' reads after every
+ * writer's kernel (for example a cross-rank barrier). n <= 7; n == 0 or
+ * peers == NULL clears. GemmEx with peers set and k == 0, or with 8-bit
+ * inputs, returns NOT_SUPPORTED. */
+grxblasStatus_t grxblasSetPeerOutputs(grxblasHandle_t handle, int n, void* const* peers);
+
 /* reference grxblas.h:131-132. Reports FP16|BF16|FP8|INT8 on B200. */
 grxblasStatus_t grxblasGetTensorTypes(grxblasHandle_t handle, unsigned* typeMask);
 

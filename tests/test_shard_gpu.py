@@ -103,3 +103,99 @@ def test_sharded_gemm_and_attention_two_gpus():
         if p.is_alive():
             p.kill()
     assert out == {0: "ok", 1: "ok"}, out
+
+
+def _fused_worker(rank, world, port, q):
+    import math
+
+    import torch.distributed as dist
+
+    from grxcp_b200 import _native as N
+    from grxcp_b200 import blas as B
+    from grxcp_b200 import shard as S
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    cbuf = None
+    try:
+        for (m, n, k) in [(512, 1024, 768), (4096, 8192, 4096)]:
+            g = torch.Generator().manual_seed(7)
+            A = (torch.randn(m * k, generator=g) / math.sqrt(k)).to(torch.bfloat16).to(dev)
+            Bm = (torch.randn(k * n, generator=g) / math.sqrt(k)).to(torch.bfloat16).to(dev)
+            bias = (torch.randn(n, generator=g) * 0.02).to(dev)
+            cbuf = S.PeerBuffer(m * n * 2, rank, world)
+            Cf = cbuf.local(torch.bfloat16)
+            Cf.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier()
+            with B.Handle() as h:
+                st = S.gemm_ex_column_parallel_fused(h, N.OP_T, N.OP_N, m, n, k, 1.0, A, N.GRX_R_16BF, k, Bm,
+                                                     N.GRX_R_16BF, k, 0.0, cbuf, N.GRX_R_16BF, m, bias=bias,
+                                                     rank=rank, world=world)
+                assert st == N.SUCCESS, N.STATUS.get(st, st)
+                assert h.execution_status() == N.SUCCESS
+                Cn = torch.zeros(m * n, device=dev, dtype=torch.bfloat16)
+                assert S.gemm_ex_column_parallel(h, N.OP_T, N.OP_N, m, n, k, 1.0, A, N.GRX_R_16BF, k, Bm,
+                                                 N.GRX_R_16BF, k, 0.0, Cn, N.GRX_R_16BF, m, bias=bias, rank=rank,
+                                                 world=world, gather=True) == N.SUCCESS
+                torch.cuda.synchronize()
+                if not torch.equal(Cf, Cn):
+                    raise AssertionError(f"fused replicated C differs from the all-gather path ({m}x{n}x{k})")
+                if m == 4096:
+                    def timed(fn, it=10):
+                        for _ in range(3):
+                            fn()
+                        torch.cuda.synchronize()
+                        dist.barrier()
+                        t0 = time.perf_counter()
+                        for _ in range(it):
+                            fn()
+                        torch.cuda.synchronize()
+                        return (time.perf_counter() - t0) / it * 1e3
+                    tf = timed(lambda: S.gemm_ex_column_parallel_fused(
+                        h, N.OP_T, N.OP_N, m, n, k, 1.0, A, N.GRX_R_16BF, k, Bm, N.GRX_R_16BF, k, 0.0, cbuf,
+                        N.GRX_R_16BF, m, bias=bias, rank=rank, world=world))
+                    tn = timed(lambda: (S.gemm_ex_column_parallel(
+                        h, N.OP_T, N.OP_N, m, n, k, 1.0, A, N.GRX_R_16BF, k, Bm, N.GRX_R_16BF, k, 0.0, Cn,
+                        N.GRX_R_16BF, m, bias=bias, rank=rank, world=world, gather=True), dist.barrier()))
+                    if rank == 0:
+                        print(f"replicated C {m}x{n}x{k} on {world} GPUs: fused {tf:.3f} ms, GEMM + all-gather "
+                              f"{tn:.3f} ms (wall clock per call incl. barrier)", flush=True)
+            dist.barrier()
+            cbuf.close()
+            cbuf = None
+        q.put((rank, "ok"))
+    except BaseException as e:
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_fused_replicated_gemm_two_gpus():
+    """Column-parallel GemmEx whose epilogue stores each rank's columns into every rank's copy of C
+    (IPC-opened peer buffers, NVLink stores): C equals the GEMM + NCCL all-gather path bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_fused_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = {}
+    deadline = time.monotonic() + 240
+    while len(out) < 2 and time.monotonic() < deadline:
+        try:
+            r, msg = q.get(timeout=1)
+            out[r] = msg
+        except Exception:
+            pass
+    for p in procs:
+        p.join(timeout=30)
+        if p.is_alive():
+            p.kill()
+    assert out == {0: "ok", 1: "ok"}, out
