@@ -210,6 +210,8 @@ PROTOTYPES: dict[str, tuple] = {
     "grxIpcGetMemHandle": (i32, [vp, vp]),
     "grxIpcOpenMemHandle": (i32, [vp, grxIpcMemHandle_t]),
     "grxIpcCloseMemHandle": (i32, [vp]),
+    "grxdnnSoftmaxBackward": (i32, [vp, i32, i32, vp, i32, i64, vp, i32, i64, vp, i32, i64]),
+    "grxdnnGeluBackward": (i32, [vp, i64, vp, vp, vp, i32, i32]),
     "grxdnnConvOutputDims": (i32, [vp, vp, vp]),
     "grxdnnConv2dForward": (i32, [vp, vp, vp, i32, vp, i32, vp, vp, vp, i32, vp, i32]),
     "grxdnnPoolingOutputDims": (i32, [vp, vp, vp]),

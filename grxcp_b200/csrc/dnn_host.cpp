@@ -257,6 +257,34 @@ grxdnnStatus_t grxdnnSoftmaxForward(grxdnnHandle_t handle, int rows, int cols, c
   return from_cuda(grx::launch_softmax(rows, cols, norm_dtype(xType), x, ldx, y, ldy, ctx.stream));
 }
 
+grxdnnStatus_t grxdnnSoftmaxBackward(grxdnnHandle_t handle, int rows, int cols, const void* y, grxDataType_t yType,
+                                     long long ldy, const void* dy, grxDataType_t dyType, long long lddy, void* dx,
+                                     grxDataType_t dxType, long long lddx) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (rows < 0 || cols < 0) return GRXDNN_STATUS_INVALID_VALUE;
+  if (rows == 0) return GRXDNN_STATUS_SUCCESS;
+  if (cols == 0 || !y || !dy || !dx || ldy < cols || lddy < cols || lddx < cols) return GRXDNN_STATUS_INVALID_VALUE;
+  if (yType != dyType || yType != dxType || norm_dtype(yType) < 0) return GRXDNN_STATUS_NOT_SUPPORTED;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  const grxdnnStatus_t s = ensure(ctx, false);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  return from_cuda(grx::launch_softmax_bwd(rows, cols, norm_dtype(yType), y, ldy, dy, lddy, dx, lddx, ctx.stream));
+}
+
+grxdnnStatus_t grxdnnGeluBackward(grxdnnHandle_t handle, long long n, const void* x, const void* dy, void* dx,
+                                  grxDataType_t type, grxdnnGeluMode_t mode) {
+  if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;
+  if (n < 0 || (unsigned)mode > 1u) return GRXDNN_STATUS_INVALID_VALUE;
+  if (n == 0) return GRXDNN_STATUS_SUCCESS;
+  if (!x || !dy || !dx) return GRXDNN_STATUS_INVALID_VALUE;
+  if (norm_dtype(type) < 0) return GRXDNN_STATUS_NOT_SUPPORTED;
+  auto& ctx = *reinterpret_cast<grxdnnContext*>(handle);
+  const grxdnnStatus_t s = ensure(ctx, false);
+  if (s != GRXDNN_STATUS_SUCCESS) return s;
+  const int act = mode == GRXDNN_GELU_ERF ? 3 /*kActGeluErf*/ : 2 /*kActGeluTanh*/;
+  return from_cuda(grx::launch_gelu_bwd(n, norm_dtype(type), x, dy, dx, act, ctx.dev.num_sms, ctx.stream));
+}
+
 grxdnnStatus_t grxdnnGeluForward(grxdnnHandle_t handle, long long n, const void* x, grxDataType_t xType, void* y,
                                  grxDataType_t yType, grxdnnGeluMode_t mode) {
   if (!handle) return GRXDNN_STATUS_NOT_INITIALIZED;

@@ -93,6 +93,10 @@ cudaError_t launch_norm_bwd(const NormBwdArgs& a, int num_sms, void* ws, size_t 
 cudaError_t launch_softmax(int rows, int cols, int dtype, const void* x, long long ldx, void* y, long long ldy,
                            cudaStream_t s);
 cudaError_t launch_gelu(long long n, int dtype, const void* x, void* y, int act, int num_sms, cudaStream_t s);
+cudaError_t launch_softmax_bwd(int rows, int cols, int dtype, const void* y, long long ldy, const void* dy,
+                               long long lddy, void* dx, long long lddx, cudaStream_t s);
+cudaError_t launch_gelu_bwd(long long n, int dtype, const void* x, const void* dy, void* dx, int act, int num_sms,
+                            cudaStream_t s);
 
 // Test hook: one CTA waits on an mbarrier nothing ever arrives at, through the
 // same bounded wait every kernel uses, and must come back with kErrTimeoutTest

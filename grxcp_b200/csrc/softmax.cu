@@ -9,6 +9,8 @@
 // once. Rows that defeat 16-byte vectors (address, pitch or width) take the
 // element-wise kernel, which reads the row three times from L2.
 // GELU is a grid-stride element-wise pass with 16-byte vectors where possible.
+// The backward kernels (softmax: dx = y (dy - sum dy y); GELU: dx = dy GELU'(x))
+// are element-wise / one-reduction passes for training.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <math.h>
@@ -176,6 +178,65 @@ cudaError_t gelu_dispatch(long long n, const void* x, void* y, int act, int num_
   return cudaGetLastError();
 }
 
+// Softmax backward, one 256-thread CTA per row: dx = y * (dy - sum_c dy y),
+// the row sum reduced in fp32 (three passes over the row, served from L1/L2
+// after the first).
+template <typename T>
+__global__ void __launch_bounds__(kThreads) softmax_bwd_kernel(int cols, const T* __restrict__ y, long long ldy,
+                                                               const T* __restrict__ dy, long long lddy,
+                                                               T* __restrict__ dx, long long lddx) {
+  __shared__ float red[64];
+  const T* yr = y + (long long)blockIdx.x * ldy;
+  const T* dr = dy + (long long)blockIdx.x * lddy;
+  T* xr = dx + (long long)blockIdx.x * lddx;
+  float s = 0.f;
+  for (int c = threadIdx.x; c < cols; c += kThreads) s = fmaf(E<T>::f(dr[c]), E<T>::f(yr[c]), s);
+  const float tot = block_reduce<false>(s, red);
+  for (int c = threadIdx.x; c < cols; c += kThreads) xr[c] = E<T>::t(E<T>::f(yr[c]) * (E<T>::f(dr[c]) - tot));
+}
+
+// GELU derivative (Hendrycks & Gimpel), times dy:
+//   erf form:  Phi(x) + x phi(x),  phi(x) = exp(-x^2 / 2) / sqrt(2 pi)
+//   tanh form: 0.5 (1 + t) + 0.5 x (1 - t^2) sqrt(2/pi) (1 + 3 * 0.044715 x^2),
+//              t = tanh(sqrt(2/pi) (x + 0.044715 x^3))
+__device__ __forceinline__ float gelu_grad(float x, int act) {
+  if (act == kActGeluErf) {
+    const float cdf = 0.5f * (1.f + erff(x * 0.7071067811865476f));
+    const float pdf = 0.3989422804014327f * expf(-0.5f * x * x);
+    return fmaf(x, pdf, cdf);
+  }
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  const float t = tanhf(k0 * fmaf(k1 * x, x * x, x));
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * fmaf(3.f * k1, x * x, 1.f);
+}
+
+template <typename T>
+__global__ void gelu_bwd_kernel(long long n, const T* __restrict__ x, const T* __restrict__ dy, T* __restrict__ dx,
+                                int act) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride)
+    dx[i] = E<T>::t(E<T>::f(dy[i]) * gelu_grad(E<T>::f(x[i]), act));
+}
+
+template <typename T>
+cudaError_t bwd_launch(int kind, long long rows_or_n, int cols, const void* a, long long lda, const void* b,
+                       long long ldb, void* c, long long ldc, int act, int num_sms, cudaStream_t s) {
+  if (kind == 0) {
+    ProfLaunch prof("softmax_bwd_kernel", dim3((unsigned)rows_or_n), dim3(kThreads), 0, s);
+    softmax_bwd_kernel<T><<<(unsigned)rows_or_n, kThreads, 0, s>>>(cols, static_cast<const T*>(a), lda,
+                                                                  static_cast<const T*>(b), ldb, static_cast<T*>(c),
+                                                                  ldc);
+  } else {
+    long long blocks = (rows_or_n + kThreads - 1) / kThreads;
+    if (blocks > (long long)num_sms * 16) blocks = (long long)num_sms * 16;
+    if (blocks < 1) blocks = 1;
+    ProfLaunch prof("gelu_bwd_kernel", dim3((unsigned)blocks), dim3(kThreads), 0, s);
+    gelu_bwd_kernel<T><<<(unsigned)blocks, kThreads, 0, s>>>(rows_or_n, static_cast<const T*>(a),
+                                                            static_cast<const T*>(b), static_cast<T*>(c), act);
+  }
+  return cudaGetLastError();
+}
+
 }  // namespace
 
 cudaError_t launch_softmax(int rows, int cols, int dtype, const void* x, long long ldx, void* y, long long ldy,
@@ -184,6 +245,26 @@ cudaError_t launch_softmax(int rows, int cols, int dtype, const void* x, long lo
     case 0: return softmax_dispatch<float>(rows, cols, x, ldx, y, ldy, s);
     case 1: return softmax_dispatch<__nv_bfloat16>(rows, cols, x, ldx, y, ldy, s);
     case 2: return softmax_dispatch<__half>(rows, cols, x, ldx, y, ldy, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_softmax_bwd(int rows, int cols, int dtype, const void* y, long long ldy, const void* dy,
+                               long long lddy, void* dx, long long lddx, cudaStream_t s) {
+  switch (dtype) {
+    case 0: return bwd_launch<float>(0, rows, cols, y, ldy, dy, lddy, dx, lddx, 0, 0, s);
+    case 1: return bwd_launch<__nv_bfloat16>(0, rows, cols, y, ldy, dy, lddy, dx, lddx, 0, 0, s);
+    case 2: return bwd_launch<__half>(0, rows, cols, y, ldy, dy, lddy, dx, lddx, 0, 0, s);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gelu_bwd(long long n, int dtype, const void* x, const void* dy, void* dx, int act, int num_sms,
+                            cudaStream_t s) {
+  switch (dtype) {
+    case 0: return bwd_launch<float>(1, n, 0, x, 0, dy, 0, dx, 0, act, num_sms, s);
+    case 1: return bwd_launch<__nv_bfloat16>(1, n, 0, x, 0, dy, 0, dx, 0, act, num_sms, s);
+    case 2: return bwd_launch<__half>(1, n, 0, x, 0, dy, 0, dx, 0, act, num_sms, s);
   }
   return cudaErrorInvalidValue;
 }

@@ -156,6 +156,16 @@ class Handle:
         d = pool_desc(x, window, pad, stride or window, mode)
         return lib.grxdnnPooling2dForward(self.h, C.byref(d), ptr(x), dtype_code(x), ptr(y), dtype_code(y))
 
+    def softmax_backward(self, y, dy, dx) -> int:
+        """grxdnnSoftmaxBackward on [rows, cols] tensors (row pitches from strides)."""
+        rows, cols = y.shape
+        return lib.grxdnnSoftmaxBackward(self.h, rows, cols, ptr(y), dtype_code(y), y.stride(0), ptr(dy),
+                                         dtype_code(dy), dy.stride(0), ptr(dx), dtype_code(dx), dx.stride(0))
+
+    def gelu_backward(self, x, dy, dx, mode: int = 0) -> int:
+        """grxdnnGeluBackward over x.numel() contiguous elements."""
+        return lib.grxdnnGeluBackward(self.h, x.numel(), ptr(x), ptr(dy), ptr(dx), dtype_code(x), mode)
+
     def attention(self, q, k, v, o, scale, causal, lse=None, descs=None) -> int:
         dq, dk, dv, do = descs if descs is not None else (attn_desc(q), attn_desc(k), attn_desc(v), attn_desc(o))
         return lib.grxdnnAttentionForward(self.h, C.byref(dq), ptr(q), C.byref(dk), ptr(k), C.byref(dv), ptr(v),

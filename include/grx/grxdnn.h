@@ -201,6 +201,21 @@ grxdnnStatus_t grxdnnPooling2dForward(grxdnnHandle_t handle, const grxdnnPoolDes
                                       const void* x, grxDataType_t xType,
                                       void* y, grxDataType_t yType);
 
+/* Softmax backward (no counterpart in the reference): from the forward's
+ * output y and the gradient dy, dx[r, c] = y[r, c] (dy[r, c] - sum_c dy y),
+ * fp32 math; y, dy, dx of one type (GRX_R_16BF, GRX_R_16F, GRX_R_32F) with
+ * row pitches >= cols. rows == 0 is SUCCESS. */
+grxdnnStatus_t grxdnnSoftmaxBackward(grxdnnHandle_t handle, int rows, int cols,
+                                     const void* y, grxDataType_t yType, long long ldy,
+                                     const void* dy, grxDataType_t dyType, long long lddy,
+                                     void* dx, grxDataType_t dxType, long long lddx);
+
+/* GELU backward (no counterpart in the reference): dx = dy * GELU'(x) for
+ * the same mode as grxdnnGeluForward; n contiguous elements, x, dy, dx of
+ * one type. n == 0 is SUCCESS. */
+grxdnnStatus_t grxdnnGeluBackward(grxdnnHandle_t handle, long long n, const void* x, const void* dy,
+                                  void* dx, grxDataType_t type, grxdnnGeluMode_t mode);
+
 grxdnnStatus_t grxdnnGetExecutionStatus(grxdnnHandle_t handle);
 
 #ifdef __cplusplus

@@ -318,6 +318,28 @@ def softmax(x):
     return y
 
 
+def softmax_bwd(y, dy):
+    """fp64 softmax backward from the forward output: dx = y (dy - sum_c dy y)."""
+    y = np.asarray(y, np.float64)
+    dy = np.asarray(dy, np.float64)
+    return y * (dy - (dy * y).sum(axis=-1, keepdims=True))
+
+
+def gelu_bwd(x, dy, mode=0):
+    """fp64 dy * GELU'(x): mode 0 erf form Phi(x) + x phi(x), 1 the tanh approximation's derivative."""
+    from math import erf, pi, sqrt
+
+    x = np.asarray(x, np.float64)
+    dy = np.asarray(dy, np.float64)
+    if mode == 0:
+        cdf = 0.5 * (1.0 + np.vectorize(erf)(x / sqrt(2.0)))
+        pdf = np.exp(-0.5 * x * x) / sqrt(2.0 * pi)
+        return dy * (cdf + x * pdf)
+    k0 = sqrt(2.0 / pi)
+    t = np.tanh(k0 * (x + 0.044715 * x ** 3))
+    return dy * (0.5 * (1.0 + t) + 0.5 * x * (1.0 - t * t) * k0 * (1.0 + 3.0 * 0.044715 * x * x))
+
+
 def gelu(x, mode=0):
     """GELU in fp64: mode 0 erf form, 1 tanh approximation."""
     x = np.ascontiguousarray(x, np.float32)

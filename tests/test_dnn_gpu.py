@@ -219,3 +219,38 @@ def test_gelu(dnn, dtype, mode, n):
     assert dnn.gelu(x, x, mode) == N.SUCCESS
     torch.cuda.synchronize()
     assert torch.equal(x, y)
+
+
+# ------------------------------------------------------------------ softmax / GELU backward
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rows,cols", [(64, 4096), (33, 1000)])
+def test_softmax_backward(dnn, dtype, rows, cols):
+    """dx = y (dy - sum dy y) against the fp64 oracle, from the library's own forward output."""
+    g = torch.Generator(device="cuda").manual_seed(rows + cols)
+    x = (torch.randn(rows, cols, device="cuda", generator=g) * 3).to(dtype)
+    dy = torch.randn(rows, cols, device="cuda", generator=g).to(dtype)
+    y = torch.empty_like(x)
+    dx = torch.full_like(x, float("nan"))
+    assert dnn.softmax(x, y) == N.SUCCESS
+    assert dnn.softmax_backward(y, dy, dx) == N.SUCCESS
+    torch.cuda.synchronize()
+    ref = oracle.softmax_bwd(y.double().cpu().numpy(), dy.double().cpu().numpy())
+    got = dx.double().cpu().numpy()
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert np.all(np.abs(got - ref) <= tol * (1e-2 + np.abs(ref)) + 1e-6), np.abs(got - ref).max()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("mode", [0, 1])
+def test_gelu_backward(dnn, dtype, mode):
+    g = torch.Generator(device="cuda").manual_seed(3 + mode)
+    x = (torch.randn(100003, device="cuda", generator=g) * 3).to(dtype)
+    dy = torch.randn(100003, device="cuda", generator=g).to(dtype)
+    dx = torch.full_like(x, float("nan"))
+    assert dnn.gelu_backward(x, dy, dx, mode) == N.SUCCESS
+    torch.cuda.synchronize()
+    ref = oracle.gelu_bwd(x.double().cpu().numpy(), dy.double().cpu().numpy(), mode)
+    got = dx.double().cpu().numpy()
+    a, r = (1e-2, 2e-2) if dtype == torch.bfloat16 else (1e-5, 1e-5)
+    assert np.all(np.abs(got - ref) <= a + r * np.abs(ref)), np.abs(got - ref).max()

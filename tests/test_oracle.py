@@ -281,3 +281,18 @@ def test_pool2d_oracle_matches_torch():
     assert np.allclose(oracle.pool2d(x, (3, 3), (1, 1), (2, 2), 0), mx)
     assert np.allclose(oracle.pool2d(x, (3, 3), (1, 1), (2, 2), 1), av)
     assert np.allclose(oracle.pool2d(x, (3, 3), (1, 1), (2, 2), 2), ex)
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+def test_softmax_gelu_backward_oracle_match_autograd(mode):
+    """The fp64 softmax / GELU backward restatements against torch autograd in fp64."""
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal((4, 37)) * 3
+    dy = rng.standard_normal((4, 37))
+    X = torch.tensor(x, requires_grad=True)
+    torch.softmax(X, -1).backward(torch.tensor(dy))
+    y = torch.softmax(torch.tensor(x), -1).numpy()
+    assert np.allclose(oracle.softmax_bwd(y, dy), X.grad.numpy(), rtol=1e-12, atol=1e-14)
+    X = torch.tensor(x, requires_grad=True)
+    torch.nn.functional.gelu(X, approximate="none" if mode == 0 else "tanh").backward(torch.tensor(dy))
+    assert np.allclose(oracle.gelu_bwd(x, dy, mode), X.grad.numpy(), rtol=1e-12, atol=1e-14)
