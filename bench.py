@@ -360,6 +360,22 @@ def run_gpu(args):
     return 0
 
 
+def _quantize_e4m3(x):
+    """[batch, rows, k] fp32 -> e4m3 codes and one scale (amax / 448) per batch member."""
+    import torch
+
+    scale = (x.abs().amax(dim=(1, 2)) / 448.0).clamp_min(1e-30)
+    return (x / scale[:, None, None]).to(torch.float8_e4m3fn), scale
+
+
+def _quantize_i8_rows(x):
+    """[batch, rows, k] fp32 -> int8 codes and one scale (amax / 127) per row, shared by the batch."""
+    import torch
+
+    scale = (x.abs().amax(dim=(0, 2)) / 127.0).clamp_min(1e-30)
+    return torch.clamp(torch.round(x / scale[None, :, None]), -127, 127).to(torch.int8), scale
+
+
 def _time(fn, iters, stream):
     import torch
 
@@ -445,11 +461,10 @@ def run_secondary(args, peaks, dev, stream):
 
     # config 5: fp8 e4m3 strided-batched MLP GEMM, batch 16, 4096 x 14336 x 4096, per-tensor scales, bf16 out
     bt, m5, n5, k5 = 16, 4096, 14336, 4096
-    a8 = (torch.randn(bt, m5, k5, device=dev, generator=g)).to(torch.float8_e4m3fn)
-    b8 = (torch.randn(bt, n5, k5, device=dev, generator=g)).to(torch.float8_e4m3fn)
+    # A/B ~ N(0,1) quantised to e4m3 with per-tensor (per batch member) scales amax / 448
+    a8, sa = _quantize_e4m3(torch.randn(bt, m5, k5, device=dev, generator=g))
+    b8, sb = _quantize_e4m3(torch.randn(bt, n5, k5, device=dev, generator=g))
     c5 = torch.empty(bt, n5, m5, device=dev, dtype=torch.bfloat16)
-    sa = torch.full((bt,), 1 / 448.0, device=dev)
-    sb = torch.full((bt,), 1 / 448.0, device=dev)
     bh.set_epilogue(scale_mode=Nn.SCALE_TENSOR, scale_a=sa, scale_b=sb, stride_scale_a=1, stride_scale_b=1)
     fl5 = 2.0 * bt * m5 * n5 * k5
     ms = _time(lambda: bh.gemm_strided_batched_ex(Nn.OP_T, Nn.OP_N, m5, n5, k5, 1.0, a8, Nn.GRX_R_8F_E4M3, k5,
@@ -461,10 +476,9 @@ def run_secondary(args, peaks, dev, stream):
                                "peak_note": "fp8 peak taken as 2x the measured bf16 peak",
                                "config": "e4m3, batch 16, 4096x14336x4096, per-tensor scales, bf16 out"}
     # int8 variant with per-row / per-column scales
-    i8a = a8.view(torch.int8)
-    i8b = b8.view(torch.int8)
-    sra = torch.full((m5,), 0.01, device=dev)
-    srb = torch.full((n5,), 0.01, device=dev)
+    # int8 codes with per-row (A) / per-column (B) scales amax / 127
+    i8a, sra = _quantize_i8_rows(torch.randn(bt, m5, k5, device=dev, generator=g))
+    i8b, srb = _quantize_i8_rows(torch.randn(bt, n5, k5, device=dev, generator=g))
     bh.set_epilogue(scale_mode=Nn.SCALE_ROWCOL, scale_a=sra, scale_b=srb)
     ms = _time(lambda: bh.gemm_strided_batched_ex(Nn.OP_T, Nn.OP_N, m5, n5, k5, 1.0, i8a, Nn.GRX_R_8I, k5,
                                                   m5 * k5, i8b, Nn.GRX_R_8I, k5, n5 * k5, 0.0, c5,
@@ -473,7 +487,7 @@ def run_secondary(args, peaks, dev, stream):
                                        "frac": fl5 / ms / 1e9 / fp8_peak,
                                        "config": "int8, batch 16, 4096x14336x4096, per-row/col scales, bf16 out"}
     bh.clear_epilogue()
-    del a8, b8, c5
+    del a8, b8, i8a, i8b, c5
     torch.cuda.empty_cache()
 
     # config 1: fp32 SGEMM 512^3 and int8 512^3
@@ -519,11 +533,10 @@ def run_profile(args):
                                   Nn.GRX_R_16BF, M))
         else:
             bt, m5, n5, k5 = 16, 4096, 14336, 4096
-            a8 = torch.randn(bt, m5, k5, device=dev, generator=g).to(torch.float8_e4m3fn)
-            b8 = torch.randn(bt, n5, k5, device=dev, generator=g).to(torch.float8_e4m3fn)
+            a8, sa = _quantize_e4m3(torch.randn(bt, m5, k5, device=dev, generator=g))
+            b8, sb = _quantize_e4m3(torch.randn(bt, n5, k5, device=dev, generator=g))
             c5 = torch.empty(bt, n5, m5, device=dev, dtype=torch.bfloat16)
-            s = torch.full((bt,), 1 / 448.0, device=dev)
-            h.set_epilogue(scale_mode=Nn.SCALE_TENSOR, scale_a=s, scale_b=s, stride_scale_a=1, stride_scale_b=1)
+            h.set_epilogue(scale_mode=Nn.SCALE_TENSOR, scale_a=sa, scale_b=sb, stride_scale_a=1, stride_scale_b=1)
             for _ in range(n_iter):
                 B.check(h.gemm_strided_batched_ex(1, 0, m5, n5, k5, 1.0, a8, Nn.GRX_R_8F_E4M3, k5, m5 * k5, b8,
                                                   Nn.GRX_R_8F_E4M3, k5, n5 * k5, 0.0, c5, Nn.GRX_R_16BF, m5,

@@ -148,6 +148,11 @@ PROTOTYPES: dict[str, tuple] = {
     "grxEventSynchronize": (i32, [vp]),
     "grxEventQuery": (i32, [vp]),
     "grxEventElapsedTime": (i32, [fp, vp, vp]),
+    # grx_tensormap.h (the desc argument is passed as an opaque pointer)
+    "grxTensorMapGetSlotCount": (i32, [C.POINTER(i32), i32]),
+    "grxMallocPhysical": (i32, [C.POINTER(vp), sz]),
+    "grxTensorMapProgramAsync": (i32, [vp, vp]),
+    "grxTensorMapProgram": (i32, [vp]),
     # grxblas.h
     "grxblasGetStatusString": (cp, [i32]),
     "grxblasCreate": (i32, [C.POINTER(vp)]),

@@ -308,6 +308,10 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
   p.group_m = 16;
   p.n_peers = ctx.n_peers;
   for (int i = 0; i < ctx.n_peers; ++i) p.peers[i] = ctx.peers[i];
+  // One probe slot per CTA of the launch, as the reference's GemmEx records
+  // one per warp (grxblas.cpp:690-694); too few slots is INVALID_VALUE.
+  p.probe = ctx.probe;
+  p.probe_capacity = ctx.probe_capacity;
   return from_cuda(grx::launch_tc_gemm(L, ctx.dev.num_sms, ctx.stream));
 }
 
@@ -455,9 +459,22 @@ grxblasStatus_t grxblasSetCycleProbe(grxblasHandle_t handle, grxCycleSlot* slots
   return GRXBLAS_STATUS_SUCCESS;
 }
 
+// Slots for an m x n call of either kernel family: the sgemm grid (at batch 1,
+// the smallest tile, so batch x this covers every batched call), or the
+// tensor-core GEMM's persistent grid, which never exceeds the SM count nor two
+// CTAs per 128 x 256 tile.
 int grxblasCycleSlotsNeeded(grxblasHandle_t handle, int m, int n) {
   (void)handle;
-  return grx::sgemm_ctas(m, n);
+  if (m <= 0 || n <= 0) return 0;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    sms = 148;  // no device: B200's count
+  }
+  const int sg = grx::sgemm_ctas(m, n, 1, sms);
+  const long long tiles = 2LL * ((m + grx::kTileM - 1) / grx::kTileM) * ((n + grx::kTileN - 1) / grx::kTileN);
+  const int tc = (int)(tiles < sms ? tiles : sms);
+  return sg > tc ? sg : tc;
 }
 
 grxblasStatus_t grxblasGetLoadedKernelPath(grxblasHandle_t handle, const char** path) {
@@ -585,7 +602,8 @@ static grxblasStatus_t sgemm_batched(grxblasHandle_t handle, grxblasOperation_t 
   std::lock_guard<std::mutex> lock(ctx.mutex);
   const grxblasStatus_t s = ensure_locked(ctx, false);
   if (s != GRXBLAS_STATUS_SUCCESS) return s;
-  if (ctx.probe && ctx.probe_capacity < grx::sgemm_ctas(m, n) * batch) return GRXBLAS_STATUS_INVALID_VALUE;
+  if (ctx.probe && ctx.probe_capacity < grx::sgemm_ctas(m, n, batch, ctx.dev.num_sms))
+    return GRXBLAS_STATUS_INVALID_VALUE;
 
   grx::SgemmArgs a{};
   a.m = m;
@@ -606,7 +624,7 @@ static grxblasStatus_t sgemm_batched(grxblasHandle_t handle, grxblasOperation_t 
   a.ldc = ldc;
   a.stride_c = strideC;
   a.probe = ctx.probe;
-  return from_cuda(grx::launch_sgemm(a, ctx.stream));
+  return from_cuda(grx::launch_sgemm(a, ctx.dev.num_sms, ctx.stream));
 }
 
 grxblasStatus_t grxblasSgemm(grxblasHandle_t handle, grxblasOperation_t transa, grxblasOperation_t transb, int m,

@@ -17,15 +17,42 @@ namespace grx {
 // sgemm.cpp:22-89): column-major, op(A)(i,l) = ta ? A[l + i*lda] : A[i + l*lda],
 // op(B)(l,j) = tb ? B[j + l*ldb] : B[l + j*ldb], batch on the grid, signed
 // element strides, beta == 0 never reads C. Instead of one thread per output
-// with two global loads per multiply-add, a 128 x 128 output tile per CTA is
-// staged through shared memory in k-slabs of 8 and each thread accumulates an
-// 8 x 8 sub-tile in registers (fp32 FMA, one accumulator per output, k in
-// ascending order).
-constexpr int SG_BM = 128, SG_BN = 128, SG_BK = 8, SG_THREADS = 256;
+// with two global loads per multiply-add, a BM x BN output tile per CTA is
+// staged through shared memory in k-slabs of BK and each thread accumulates a
+// TM x TN sub-tile in registers (fp32 FMA, one accumulator per output, k in
+// ascending order, so every tile shape gives the same bits).
+//
+// The slabs stream through an ST-deep cp.async ring (4-byte copies with
+// zero fill past the matrix edge), so the global-load latency of slab t + ST - 1
+// overlaps the FMAs of slab t; a k-step no longer waits a full memory round
+// trip. The tile shape follows the grid: 128 x 128 once that fills the SMs,
+// else 64 x 64, else 32 x 32 (a 512^3 problem is 16 CTAs of 128 x 128 but 256
+// of 32 x 32).
+template <int BM, int BN, int BK, int TM, int TN, int ST>
+struct SgemmCfg {
+  static constexpr int kThreads = (BM / TM) * (BN / TN);
+  static constexpr int kGx = BM / TM;  // threads along m
+  static constexpr int kPadM = BM + 4, kPadN = BN + 4;  // +4 floats: the k-fastest fill is conflict-free
+};
 
-__global__ void __launch_bounds__(SG_THREADS) sgemm_kernel(SgemmArgs p) {
-  __shared__ __align__(16) float As[2][SG_BK][SG_BM];
-  __shared__ __align__(16) float Bs[2][SG_BK][SG_BN];
+__device__ __forceinline__ void cp_async4(float* smem, const float* g, bool pred) {
+  const uint32_t s = smem_u32(smem);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s), "l"(g), "r"(pred ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <int BM, int BN, int BK, int TM, int TN, int ST>
+__global__ void __launch_bounds__(SgemmCfg<BM, BN, BK, TM, TN, ST>::kThreads) sgemm_kernel(SgemmArgs p) {
+  using Cfg = SgemmCfg<BM, BN, BK, TM, TN, ST>;
+  constexpr int NT = Cfg::kThreads;
+  static_assert((BM * BK) % NT == 0 && (BN * BK) % NT == 0, "slab must split evenly over the threads");
+  static_assert(TM % 4 == 0 && TN % 4 == 0, "sub-tiles are read as float4 groups");
+  __shared__ __align__(16) float As[ST][BK][Cfg::kPadM];
+  __shared__ __align__(16) float Bs[ST][BK][Cfg::kPadN];
   long long t_start = 0;
   if (p.probe) t_start = clock64();
 
@@ -33,67 +60,84 @@ __global__ void __launch_bounds__(SG_THREADS) sgemm_kernel(SgemmArgs p) {
   const float* A = p.a + (long long)bz * p.stride_a;
   const float* B = p.b + (long long)bz * p.stride_b;
   float* C = p.c + (long long)bz * p.stride_c;
-  const int m0 = blockIdx.x * SG_BM, n0 = blockIdx.y * SG_BN;
+  const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
   const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;
+  const int tx = tid % Cfg::kGx, ty = tid / Cfg::kGx;
 
-  // Load mapping: 1024 elements per operand slab, 4 per thread. The fastest
-  // index follows the operand's contiguous direction.
-  auto load_slab = [&](int buf, int k0) {
+  // One slab: element (r, l) of op(A) to As[slot][l][r], (l, c) of op(B) to
+  // Bs[slot][l][c]. Consecutive threads take the operand's contiguous direction.
+  auto issue = [&](int slot, int k0) {
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int idx = tid + e * SG_THREADS;
-      int r, l;  // A: r in [0,128) rows of op(A), l in [0,8)
-      if (!p.ta) { r = idx & 127; l = idx >> 7; } else { l = idx & 7; r = idx >> 3; }
+    for (int e = 0; e < BM * BK / NT; ++e) {
+      const int idx = tid + e * NT;
+      int r, l;
+      if (!p.ta) { r = idx % BM; l = idx / BM; } else { l = idx % BK; r = idx / BK; }
       const int gi = m0 + r, gl = k0 + l;
-      float v = 0.f;
-      if (gi < p.m && gl < p.k) v = p.ta ? A[gl + (long long)gi * p.lda] : A[gi + (long long)gl * p.lda];
-      As[buf][l][r] = v;
-      int c, lb;  // B: c in [0,128) columns of op(B)
-      if (!p.tb) { lb = idx & 7; c = idx >> 3; } else { c = idx & 127; lb = idx >> 7; }
-      const int gj = n0 + c, gl2 = k0 + lb;
-      float w = 0.f;
-      if (gj < p.n && gl2 < p.k) w = p.tb ? B[gj + (long long)gl2 * p.ldb] : B[gl2 + (long long)gj * p.ldb];
-      Bs[buf][lb][c] = w;
+      const bool ok = gi < p.m && gl < p.k;
+      const float* src = !ok ? A : (p.ta ? A + gl + (long long)gi * p.lda : A + gi + (long long)gl * p.lda);
+      cp_async4(&As[slot][l][r], src, ok);
+    }
+#pragma unroll
+    for (int e = 0; e < BN * BK / NT; ++e) {
+      const int idx = tid + e * NT;
+      int c, l;
+      if (!p.tb) { l = idx % BK; c = idx / BK; } else { c = idx % BN; l = idx / BN; }
+      const int gj = n0 + c, gl = k0 + l;
+      const bool ok = gj < p.n && gl < p.k;
+      const float* src = !ok ? B : (p.tb ? B + gj + (long long)gl * p.ldb : B + gl + (long long)gj * p.ldb);
+      cp_async4(&Bs[slot][l][c], src, ok);
     }
   };
 
-  float acc[8][8];
+  float acc[TM][TN];
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+  for (int i = 0; i < TM; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.f;
 
-  const int kt = (p.k + SG_BK - 1) / SG_BK;
-  if (kt > 0) load_slab(0, 0);
-  __syncthreads();
-  for (int t = 0; t < kt; ++t) {
-    const int cur = t & 1;
-    if (t + 1 < kt) load_slab(cur ^ 1, (t + 1) * SG_BK);
+  // Row of sub-tile entry i: groups of 4 rows spaced BM / (TM / 4) apart.
+  constexpr int RS = BM * 4 / TM, CS = BN * 4 / TN;
+  const int kt = (p.k + BK - 1) / BK;
 #pragma unroll
-    for (int l = 0; l < SG_BK; ++l) {
-      float a[8], b[8];
-      const float4 a0 = *reinterpret_cast<const float4*>(&As[cur][l][tx * 4]);
-      const float4 a1 = *reinterpret_cast<const float4*>(&As[cur][l][64 + tx * 4]);
-      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[cur][l][ty * 4]);
-      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[cur][l][64 + ty * 4]);
-      a[0] = a0.x; a[1] = a0.y; a[2] = a0.z; a[3] = a0.w; a[4] = a1.x; a[5] = a1.y; a[6] = a1.z; a[7] = a1.w;
-      b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w; b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-    }
-    __syncthreads();
+  for (int s = 0; s < ST - 1; ++s) {
+    if (s < kt) issue(s, s * BK);
+    cp_async_commit();
   }
+  for (int t = 0; t < kt; ++t) {
+    cp_async_wait<ST - 2>();
+    __syncthreads();  // slab t landed for every thread; slab t - 1's slot is free
+    const int nt = t + ST - 1;
+    if (nt < kt) issue(nt % ST, nt * BK);
+    cp_async_commit();
+    const int cur = t % ST;
+#pragma unroll
+    for (int l = 0; l < BK; ++l) {
+      float a[TM], b[TN];
+#pragma unroll
+      for (int g = 0; g < TM / 4; ++g) {
+        const float4 v = *reinterpret_cast<const float4*>(&As[cur][l][g * RS + tx * 4]);
+        a[g * 4 + 0] = v.x; a[g * 4 + 1] = v.y; a[g * 4 + 2] = v.z; a[g * 4 + 3] = v.w;
+      }
+#pragma unroll
+      for (int g = 0; g < TN / 4; ++g) {
+        const float4 v = *reinterpret_cast<const float4*>(&Bs[cur][l][g * CS + ty * 4]);
+        b[g * 4 + 0] = v.x; b[g * 4 + 1] = v.y; b[g * 4 + 2] = v.z; b[g * 4 + 3] = v.w;
+      }
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+  }
+  cp_async_wait<0>();
 
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int gj = n0 + (j < 4 ? ty * 4 + j : 64 + ty * 4 + (j - 4));
+  for (int j = 0; j < TN; ++j) {
+    const int gj = n0 + (j / 4) * CS + ty * 4 + (j % 4);
     if (gj >= p.n) continue;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int gi = m0 + (i < 4 ? tx * 4 + i : 64 + tx * 4 + (i - 4));
+    for (int i = 0; i < TM; ++i) {
+      const int gi = m0 + (i / 4) * RS + tx * 4 + (i % 4);
       if (gi >= p.m) continue;
       const long long ci = gi + (long long)gj * p.ldc;
       const float v = __fmul_rn(p.alpha, acc[i][j]);
@@ -114,17 +158,38 @@ __global__ void __launch_bounds__(SG_THREADS) sgemm_kernel(SgemmArgs p) {
   }
 }
 
-int sgemm_ctas(int m, int n) {
-  if (m <= 0 || n <= 0) return 0;
-  return ((m + SG_BM - 1) / SG_BM) * ((n + SG_BN - 1) / SG_BN);
+// Square tile edge for an m x n x batch problem: the largest of 128 / 64 / 32
+// whose grid reaches one CTA per SM, else 32.
+int sgemm_tile(int m, int n, int batch, int num_sms) {
+  for (int t : {128, 64}) {
+    const long long ctas = (long long)((m + t - 1) / t) * ((n + t - 1) / t) * (batch > 0 ? batch : 1);
+    if (ctas >= num_sms) return t;
+  }
+  return 32;
 }
 
-cudaError_t launch_sgemm(const SgemmArgs& a, cudaStream_t s) {
-  dim3 grid((a.m + SG_BM - 1) / SG_BM, (a.n + SG_BN - 1) / SG_BN, a.batch);
+int sgemm_ctas(int m, int n, int batch, int num_sms) {
+  if (m <= 0 || n <= 0 || batch <= 0) return 0;
+  const int t = sgemm_tile(m, n, batch, num_sms);
+  return ((m + t - 1) / t) * ((n + t - 1) / t) * batch;
+}
+
+template <int BM, int BK, int TM, int ST>
+static cudaError_t sgemm_go(const SgemmArgs& a, cudaStream_t s) {
+  constexpr int NT = SgemmCfg<BM, BM, BK, TM, TM, ST>::kThreads;
+  dim3 grid((a.m + BM - 1) / BM, (a.n + BM - 1) / BM, a.batch);
   if (grid.y > 65535u || grid.z > 65535u) return cudaErrorInvalidValue;
-  ProfLaunch prof("sgemm_kernel", grid, dim3(SG_THREADS), 0, s);
-  sgemm_kernel<<<grid, SG_THREADS, 0, s>>>(a);
+  ProfLaunch prof("sgemm_kernel", grid, dim3(NT), 0, s);
+  sgemm_kernel<BM, BM, BK, TM, TM, ST><<<grid, NT, 0, s>>>(a);
   return cudaGetLastError();
+}
+
+cudaError_t launch_sgemm(const SgemmArgs& a, int num_sms, cudaStream_t s) {
+  switch (sgemm_tile(a.m, a.n, a.batch, num_sms)) {
+    case 128: return sgemm_go<128, 8, 8, 4>(a, s);
+    case 64: return sgemm_go<64, 16, 4, 4>(a, s);
+    default: return sgemm_go<32, 16, 4, 4>(a, s);
+  }
 }
 
 // ---------------------------------------------------------------- packing

@@ -115,10 +115,13 @@ extern "C" grxblasStatus_t grxblasGemmExNoAlloc(grxStream_t stream, grxblasOpera
     kind = grx::kKindF16; fmt = 0; es = 2; out = Ctype == GRX_R_32F ? grx::kOutF32 : grx::kOutF16;
   } else if (Atype == GRX_R_16BF && (Ctype == GRX_R_32F || Ctype == GRX_R_16BF)) {
     kind = grx::kKindF16; fmt = 1; es = 2; out = Ctype == GRX_R_32F ? grx::kOutF32 : grx::kOutBF16;
-  } else if (Atype == GRX_R_8I && Ctype == GRX_R_32I) {
-    kind = grx::kKindI8; fmt = 1; es = 1; out = grx::kOutS32;
+  } else if (Atype == GRX_R_8I && (Ctype == GRX_R_32I || Ctype == GRX_R_16BF || Ctype == GRX_R_32F)) {
+    kind = grx::kKindI8; fmt = 1; es = 1;
+    out = Ctype == GRX_R_32I ? grx::kOutS32 : (Ctype == GRX_R_16BF ? grx::kOutBF16 : grx::kOutF32);
+    // The exact int32 output takes integer alpha/beta only (reference
+    // grxblas.cpp:580-584); the float outputs take any.
     const float a = *alpha, b = *beta;
-    if (a != (float)(int)a || b != (float)(int)b) return GRXBLAS_STATUS_INVALID_VALUE;
+    if (out == grx::kOutS32 && (a != (float)(int)a || b != (float)(int)b)) return GRXBLAS_STATUS_INVALID_VALUE;
   } else if (Atype == GRX_R_8F_E4M3 && (Ctype == GRX_R_32F || Ctype == GRX_R_16BF)) {
     kind = grx::kKindF8; fmt = 0; es = 1; out = Ctype == GRX_R_32F ? grx::kOutF32 : grx::kOutBF16;
   } else {

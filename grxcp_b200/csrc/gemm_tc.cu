@@ -443,6 +443,19 @@ __device__ __forceinline__ void epilogue_conv(const TcGemmParams& p, uint32_t t_
   }
 }
 
+// Cycle-probe record of this CTA (grxblasSetCycleProbe); thread 0 only.
+__device__ __forceinline__ void probe_write(const TcGemmParams& p, uint64_t t0) {
+  if (p.probe == nullptr || threadIdx.x != 0 || (int)blockIdx.x >= p.probe_capacity) return;
+  unsigned smid;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+  grxCycleSlot s;
+  s.start = t0;
+  s.end = (uint64_t)clock64();
+  s.core = smid;
+  s.warp = blockIdx.x;
+  p.probe[blockIdx.x] = s;
+}
+
 template <int KIND, int OUT, bool CONV, bool PEER>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -458,6 +471,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (threadIdx.x == 0 && p.err_word) atomicCAS(p.err_word, 0, kErrBadAbi);
     return;
   }
+  const uint64_t probe_t0 = p.probe ? clock64() : 0ull;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -674,6 +688,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * kTileN);
   }
+  probe_write(p, probe_t0);
 }
 
 // CTA-pair kernel. Cluster of two CTAs (rank 0 = leader). Each CTA:
@@ -703,6 +718,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     if (threadIdx.x == 0 && p.err_word) atomicCAS(p.err_word, 0, kErrBadAbi);
     return;  // both CTAs of every pair take this branch alike
   }
+  const uint64_t probe_t0 = p.probe ? clock64() : 0ull;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -873,6 +889,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, 2 * kPairTileN);
   }
+  probe_write(p, probe_t0);
 }
 
 // ---------------------------------------------------------------- host side
@@ -1176,6 +1193,7 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
   if (pair) {
     const int pairs = (int)(tiles < num_sms / 2 ? tiles : num_sms / 2);
     const int g2 = 2 * pairs;
+    if (p.probe && p.probe_capacity < g2) return cudaErrorInvalidValue;
     if (p.n_peers > 0) {
       switch (L.out) {
         case kOutF32: return launch_pair_impl<kKindF16, kOutF32, true>(ma, mb, p, g2, stream);
@@ -1213,6 +1231,7 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
     const long long units = sp.dp_tiles + sp.sk_tiles * sp.splits;
     grid = (int)(units < num_sms ? units : num_sms);
   }
+  if (p.probe && p.probe_capacity < grid) return cudaErrorInvalidValue;
   if (p.n_peers > 0) {
     switch (L.out) {
       case kOutF32: return launch_impl<kKindF16, kOutF32, false, true>(ma, mb, p, grid, stream);

@@ -5,13 +5,15 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "grx/grx_cycles.h"
+
 namespace grx {
 
 // Versioned argument block, passed by value as a __grid_constant__ parameter.
 // The kernel refuses to run on a version mismatch (the reference's kernel ABI
 // blocks do the same, src/libs/grxblas/hgemm_abi.h:20 and
 // src/libs/grxblas/kernels/sgemm.cpp:23-27).
-constexpr uint32_t kTcGemmAbi = 6;
+constexpr uint32_t kTcGemmAbi = 7;
 constexpr int kMaxPeers = 7;  // one process per GPU, eight GPUs per node
 
 enum TcKind : int { kKindF16 = 0, kKindI8 = 1, kKindF8 = 2 };
@@ -65,6 +67,11 @@ struct TcGemmParams {
   // offset in peers[0 .. n_peers) (other GPUs' buffers opened in this process).
   int n_peers;
   void* peers[kMaxPeers];
+  // Cycle probe (grxblasSetCycleProbe): when set, thread 0 of CTA b writes
+  // probe[b] (clock64 at entry and exit, %smid, b). The host checks that
+  // probe_capacity covers the grid before launching.
+  grxCycleSlot* probe;
+  int probe_capacity;
 };
 
 struct TcGemmLaunch {

@@ -18,9 +18,10 @@ struct SgemmArgs {
   float* c; long long ldc, stride_c;
   grxCycleSlot* probe;  // one slot per CTA, or null
 };
-cudaError_t launch_sgemm(const SgemmArgs& a, cudaStream_t s);
-// CTAs the sgemm kernel launches for an m x n problem (one probe slot each).
-int sgemm_ctas(int m, int n);
+cudaError_t launch_sgemm(const SgemmArgs& a, int num_sms, cudaStream_t s);
+// CTAs the sgemm kernel launches for an m x n x batch problem on num_sms SMs
+// (one probe slot each).
+int sgemm_ctas(int m, int n, int batch, int num_sms);
 
 // Copies op(X) (R rows of the MN extent by K) into a dense K-major buffer
 // dst[b][r][kk] with row pitch ldp elements. es = element bytes (1 or 2).

@@ -9,6 +9,7 @@
 #include <string.h>
 
 #include "grx/grx_runtime.h"
+#include "grx/grx_tensormap.h"
 
 namespace {
 
@@ -301,5 +302,24 @@ grxError_t grxEventElapsedTime(float* ms, grxEvent_t a, grxEvent_t b) {
   if (!ms) return rec_g(grxErrorInvalidValue);
   return rec(cudaEventElapsedTime(ms, ce(a), ce(b)));
 }
+
+// Tensor maps (reference grx_tensormap.h:78-108). B200 has no descriptor slots:
+// a TMA descriptor is a per-launch kernel parameter, so there is nothing to
+// program and the slot count is 0.
+grxError_t grxTensorMapGetSlotCount(int* count, int device) {
+  if (!count) return rec_g(grxErrorInvalidValue);
+  int n = 0;
+  const cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) return rec(e);
+  if (device < 0 || device >= n) return rec_g(grxErrorInvalidDevice);
+  *count = 0;
+  return grxSuccess;
+}
+grxError_t grxMallocPhysical(void** ptr, size_t size) { return grxMalloc(ptr, size); }
+grxError_t grxTensorMapProgramAsync(const grxTensorMapDesc_t* desc, grxStream_t) {
+  if (!desc) return rec_g(grxErrorInvalidValue);
+  return rec_g(grxErrorNotSupported);
+}
+grxError_t grxTensorMapProgram(const grxTensorMapDesc_t* desc) { return grxTensorMapProgramAsync(desc, nullptr); }
 
 }  // extern "C"

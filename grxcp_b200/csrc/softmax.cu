@@ -60,8 +60,8 @@ __device__ __forceinline__ float block_reduce(float v, float* red) {
 }
 
 template <typename T, int NV>
-__global__ void __launch_bounds__(kThreads) softmax_vec_kernel(int cols, const T* __restrict__ x, long long ldx,
-                                                              T* __restrict__ y, long long ldy) {
+__global__ void __launch_bounds__(kThreads) softmax_vec_kernel(int cols, const T* x, long long ldx,
+                                                              T* y, long long ldy) {
   constexpr int EPV = 16 / sizeof(T);
   __shared__ float red[64];
   const long long row = blockIdx.x;
@@ -107,8 +107,8 @@ __global__ void __launch_bounds__(kThreads) softmax_vec_kernel(int cols, const T
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads) softmax_scalar_kernel(int cols, const T* __restrict__ x, long long ldx,
-                                                                 T* __restrict__ y, long long ldy) {
+__global__ void __launch_bounds__(kThreads) softmax_scalar_kernel(int cols, const T* x, long long ldx,
+                                                                 T* y, long long ldy) {
   __shared__ float red[64];
   const T* xr = x + (long long)blockIdx.x * ldx;
   T* yr = y + (long long)blockIdx.x * ldy;
@@ -146,7 +146,7 @@ cudaError_t softmax_dispatch(int rows, int cols, const void* x, long long ldx, v
 }
 
 template <typename T>
-__global__ void gelu_kernel(long long n, const T* __restrict__ x, T* __restrict__ y, int act, int vec) {
+__global__ void gelu_kernel(long long n, const T* x, T* y, int act, int vec) {
   constexpr int EPV = 16 / sizeof(T);
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -182,9 +182,9 @@ cudaError_t gelu_dispatch(long long n, const void* x, void* y, int act, int num_
 // the row sum reduced in fp32 (three passes over the row, served from L1/L2
 // after the first).
 template <typename T>
-__global__ void __launch_bounds__(kThreads) softmax_bwd_kernel(int cols, const T* __restrict__ y, long long ldy,
-                                                               const T* __restrict__ dy, long long lddy,
-                                                               T* __restrict__ dx, long long lddx) {
+__global__ void __launch_bounds__(kThreads) softmax_bwd_kernel(int cols, const T* y, long long ldy,
+                                                               const T* dy, long long lddy,
+                                                               T* dx, long long lddx) {
   __shared__ float red[64];
   const T* yr = y + (long long)blockIdx.x * ldy;
   const T* dr = dy + (long long)blockIdx.x * lddy;
@@ -211,7 +211,7 @@ __device__ __forceinline__ float gelu_grad(float x, int act) {
 }
 
 template <typename T>
-__global__ void gelu_bwd_kernel(long long n, const T* __restrict__ x, const T* __restrict__ dy, T* __restrict__ dx,
+__global__ void gelu_bwd_kernel(long long n, const T* x, const T* dy, T* dx,
                                 int act) {
   const long long stride = (long long)gridDim.x * blockDim.x;
   for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride)

@@ -160,8 +160,13 @@ def gemm_ex_column_parallel_fused(handle, transa, transb, m, n, k, alpha, A, Aty
     """Column-parallel GemmEx whose epilogue writes this rank's columns into
     every rank's copy of C (cbuf, a PeerBuffer holding the full ldc x n C):
     the replicated-output step fused into the GEMM over NVLink instead of a
-    separate all-gather. Ends with a barrier, after which C is complete on
-    every rank. 16-bit inputs only (grxblasSetPeerOutputs)."""
+    separate all-gather. 16-bit inputs only (grxblasSetPeerOutputs).
+
+    Ordering: the call starts with a barrier (after this rank's stream has
+    drained), so no peer stores into this rank's C while this rank may still
+    be reading the previous contents, and ends with a device synchronise
+    followed by a barrier, so on return C is complete on every rank whatever
+    the process group's backend (a gloo barrier does not order GPU work)."""
     import torch
     import torch.distributed as dist
 
@@ -177,6 +182,10 @@ def gemm_ex_column_parallel_fused(handle, transa, transb, m, n, k, alpha, A, Aty
         st = handle.set_epilogue(bias=bv, bias_type=N.GRX_R_32F if bias.dtype.itemsize == 4 else N.GRX_R_16BF)
         if st != N.SUCCESS:
             return st
+    if world > 1:
+        # Entry barrier: every rank has finished with cbuf's previous contents.
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
     try:
         if cols.count > 0:
             st = handle.gemm_ex(transa, transb, m, cols.count, k, alpha, A, Atype, lda, b, Btype, ldb, beta, c, Ctype,
@@ -185,11 +194,12 @@ def gemm_ex_column_parallel_fused(handle, transa, transb, m, n, k, alpha, A, Aty
         handle.set_peer_outputs([])
         if bias is not None:
             handle.clear_epilogue()
-    if st == N.SUCCESS and world > 1:
-        # Every rank's kernel (and its stores into the other copies) precedes
-        # its part of this collective on the same stream.
-        dist.barrier(group=group)
+    if world > 1:
+        # This rank's kernel, and its stores into the other copies, completes
+        # before the rank enters the barrier. Entered on failure too, so that
+        # no rank is left waiting for one that returned early.
         torch.cuda.synchronize()
+        dist.barrier(group=group)
     return st
 
 

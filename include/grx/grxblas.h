@@ -20,6 +20,7 @@
 
 #include "grx_cycles.h"
 #include "grx_runtime.h"
+#include "grx_tensormap.h"
 #include "grx_types.h"
 
 #ifdef __cplusplus

@@ -92,7 +92,8 @@ grxdnnStatus_t grxdnnLayerNormBackward(grxdnnHandle_t handle, int rows, int hidd
 /* Softmax over the last dimension of a [rows, cols] matrix:
  *   y[r, c] = exp(x[r, c] - max_c x[r, :]) / sum_c exp(x[r, c] - max_c x[r, :])
  * in fp32. x/y of the same type (GRX_R_16BF, GRX_R_16F or GRX_R_32F), row
- * pitches ldx/ldy >= cols. rows == 0 is SUCCESS. */
+ * pitches ldx/ldy >= cols. rows == 0 is SUCCESS. y may alias x (in place,
+ * with ldy == ldx). */
 grxdnnStatus_t grxdnnSoftmaxForward(grxdnnHandle_t handle, int rows, int cols,
                                     const void* x, grxDataType_t xType, long long ldx,
                                     void* y, grxDataType_t yType, long long ldy);
@@ -204,7 +205,8 @@ grxdnnStatus_t grxdnnPooling2dForward(grxdnnHandle_t handle, const grxdnnPoolDes
 /* Softmax backward (no counterpart in the reference): from the forward's
  * output y and the gradient dy, dx[r, c] = y[r, c] (dy[r, c] - sum_c dy y),
  * fp32 math; y, dy, dx of one type (GRX_R_16BF, GRX_R_16F, GRX_R_32F) with
- * row pitches >= cols. rows == 0 is SUCCESS. */
+ * row pitches >= cols. rows == 0 is SUCCESS. dx may alias dy or y (in place,
+ * with equal pitches). */
 grxdnnStatus_t grxdnnSoftmaxBackward(grxdnnHandle_t handle, int rows, int cols,
                                      const void* y, grxDataType_t yType, long long ldy,
                                      const void* dy, grxDataType_t dyType, long long lddy,
@@ -212,7 +214,7 @@ grxdnnStatus_t grxdnnSoftmaxBackward(grxdnnHandle_t handle, int rows, int cols,
 
 /* GELU backward (no counterpart in the reference): dx = dy * GELU'(x) for
  * the same mode as grxdnnGeluForward; n contiguous elements, x, dy, dx of
- * one type. n == 0 is SUCCESS. */
+ * one type. n == 0 is SUCCESS. dx may alias dy or x. */
 grxdnnStatus_t grxdnnGeluBackward(grxdnnHandle_t handle, long long n, const void* x, const void* dy,
                                   void* dx, grxDataType_t type, grxdnnGeluMode_t mode);
 

@@ -239,6 +239,14 @@ def test_softmax_backward(dnn, dtype, rows, cols):
     got = dx.double().cpu().numpy()
     tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
     assert np.all(np.abs(got - ref) <= tol * (1e-2 + np.abs(ref)) + 1e-6), np.abs(got - ref).max()
+    # in place (dx aliasing dy, as training code does): the same bits as out of place
+    dy2 = dy.clone()
+    assert dnn.softmax_backward(y, dy2, dy2) == N.SUCCESS
+    y2 = x.clone()
+    assert dnn.softmax(y2, y2) == N.SUCCESS
+    torch.cuda.synchronize()
+    assert torch.equal(dy2, dx)
+    assert torch.equal(y2, y)
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
@@ -254,3 +262,8 @@ def test_gelu_backward(dnn, dtype, mode):
     got = dx.double().cpu().numpy()
     a, r = (1e-2, 2e-2) if dtype == torch.bfloat16 else (1e-5, 1e-5)
     assert np.all(np.abs(got - ref) <= a + r * np.abs(ref)), np.abs(got - ref).max()
+    # in place (dx aliasing dy): the same bits as out of place
+    dy2 = dy.clone()
+    assert dnn.gelu_backward(x, dy2, dy2, mode) == N.SUCCESS
+    torch.cuda.synchronize()
+    assert torch.equal(dy2, dx)

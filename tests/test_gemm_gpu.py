@@ -427,3 +427,73 @@ def test_epilogue_activation_refused_for_exact_int8(blas):
     assert blas.gemm_ex(0, 0, 8, 4, 16, 1.0, d, N.GRX_R_8I, 8, d, N.GRX_R_8I, 16, 0.0, c, N.GRX_R_32I, 8) == \
         N.NOT_SUPPORTED
     assert blas.set_epilogue(activation=9) == N.INVALID_VALUE
+
+
+# ------------------------------------------------------------------ config 5 at full size
+
+def _quantize_e4m3_per_tensor(x):
+    """x [batch, rows, k] fp32 -> (e4m3 codes, per-batch-member scale amax / 448)."""
+    amax = x.abs().amax(dim=(1, 2)).clamp_min(1e-30)
+    scale = (amax / 448.0).float()
+    return (x / scale[:, None, None]).to(torch.float8_e4m3fn), scale
+
+
+def _config5_columns(n, batch_member):
+    rng = np.random.default_rng(100 + batch_member)
+    return np.unique(np.concatenate([[0, 1, 255, 256, n - 1], rng.integers(0, n, 11)]))
+
+
+@pytest.mark.parametrize("kind", ["fp8_per_tensor", "int8_rowcol"])
+def test_config5_full_size_sampled(blas, kind):
+    """BASELINE config 5 at its real size: batch 16 x M=4096 x N=14336 x K=4096,
+    A/B ~ N(0,1) quantised (e4m3 with per-tensor amax/448 scales, or int8 with
+    per-row / per-column amax/127 scales), fp32 accumulate, bf16 out through the
+    fused scale epilogue. 16 full output columns (first, last, tile seams, random)
+    of batch members 0, 7 and 15 are checked against the fp64 oracle of the
+    dequantised inputs within 1e-2 + 2e-2 |ref|."""
+    bt, m, n, k = 16, 4096, 14336, 4096
+    g = torch.Generator(device="cuda").manual_seed(55)
+    af = torch.randn(bt, m, k, device="cuda", generator=g)
+    if kind == "fp8_per_tensor":
+        a8, sa = _quantize_e4m3_per_tensor(af)
+        del af
+        bf = torch.randn(bt, n, k, device="cuda", generator=g)
+        b8, sb = _quantize_e4m3_per_tensor(bf)
+        del bf
+        atype = N.GRX_R_8F_E4M3
+        assert blas.set_epilogue(scale_mode=N.SCALE_TENSOR, scale_a=sa, scale_b=sb, stride_scale_a=1,
+                                 stride_scale_b=1) == N.SUCCESS
+    else:
+        # per-row scales of op(A) and per-column of op(B), shared by the batch (stride 0)
+        sa = (af.abs().amax(dim=(0, 2)) / 127).clamp_min(1e-30)
+        a8 = torch.clamp(torch.round(af / sa[None, :, None]), -127, 127).to(torch.int8)
+        del af
+        bf = torch.randn(bt, n, k, device="cuda", generator=g)
+        sb = (bf.abs().amax(dim=(0, 2)) / 127).clamp_min(1e-30)
+        b8 = torch.clamp(torch.round(bf / sb[None, :, None]), -127, 127).to(torch.int8)
+        del bf
+        atype = N.GRX_R_8I
+        assert blas.set_epilogue(scale_mode=N.SCALE_ROWCOL, scale_a=sa, scale_b=sb) == N.SUCCESS
+    c = torch.empty(bt, n, m, device="cuda", dtype=torch.bfloat16)
+    st = blas.gemm_strided_batched_ex(1, 0, m, n, k, 1.0, a8, atype, k, m * k, b8, atype, k, n * k, 0.0, c,
+                                      N.GRX_R_16BF, m, m * n, bt)
+    assert st == N.SUCCESS
+    torch.cuda.synchronize()
+    assert blas.execution_status() == N.SUCCESS
+    blas.clear_epilogue()
+    for bi in (0, 7, 15):
+        cols = _config5_columns(n, bi)
+        idx = torch.as_tensor(cols, device="cuda")
+        A = a8[bi].float().cpu().numpy().ravel()  # codes as values (e4m3 decodes exactly to fp32)
+        Bsub = b8[bi][idx].float().cpu().numpy().ravel()
+        if kind == "fp8_per_tensor":
+            want = oracle.gemm_f64(1, 0, m, len(cols), k, 1.0, A, k, Bsub, k, scale_mode=1,
+                                   sa=sa[bi:bi + 1].cpu().numpy(), sb=sb[bi:bi + 1].cpu().numpy())
+        else:
+            want = oracle.gemm_f64(1, 0, m, len(cols), k, 1.0, A, k, Bsub, k, scale_mode=2, sa=sa.cpu().numpy(),
+                                   sb=sb[idx].cpu().numpy())
+        got = c[bi][idx].float().cpu().numpy().ravel()
+        ok, nbad = close(got, want)
+        assert ok, f"batch {bi}: {nbad} of {got.size} out of tolerance"
+    del a8, b8, c
+    torch.cuda.empty_cache()
