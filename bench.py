@@ -269,7 +269,13 @@ def run_gpu(args):
     # steps are pipelined the way a serving loop would run them: step i+1's
     # uploads (copy stream 1) overlap step i's GEMM (compute stream) and its
     # download (copy stream 2), with double-buffered device tensors.
-    hA = A.cpu().pin_memory()
+    # Column-parallel wants A replicated: each rank uploads only its 1/world of
+    # A's rows (stored k x m, so a row band of op(A) is contiguous) and one NCCL
+    # all-gather over NVLink assembles A in every rank's HBM; host links carry
+    # A once per step in total instead of once per rank.
+    assert M % world == 0
+    mrows = M // world
+    hA = A[rank * mrows:(rank + 1) * mrows].cpu().pin_memory()
     hB = Bl.cpu().pin_memory()
     hbias = bias.cpu().pin_memory()
     hC = [torch.empty(nl, M, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
@@ -287,7 +293,14 @@ def run_gpu(args):
         bsel = i & 1
         with torch.cuda.stream(up):
             up.wait_event(gemm_done[bsel])  # the GEMM that last read these buffers is done
-            dA[bsel].copy_(hA, non_blocking=True)
+            if world > 1:
+                import torch.distributed as dist
+
+                mine = dA[bsel][rank * mrows:(rank + 1) * mrows]
+                mine.copy_(hA, non_blocking=True)
+                dist.all_gather_into_tensor(dA[bsel], mine)  # on the upload stream (torch's current here)
+            else:
+                dA[bsel].copy_(hA, non_blocking=True)
             dB[bsel].copy_(hB, non_blocking=True)
             dbias[bsel].copy_(hbias, non_blocking=True)
             h2d_done[bsel].record(up)
@@ -319,15 +332,18 @@ def run_gpu(args):
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
-    h2d = (A.numel() + Bl.numel()) * 2 + bias.numel() * 4
+    h2d = (hA.numel() + Bl.numel()) * 2 + bias.numel() * 4
     d2h = C.numel() * 2
     e2e = {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world,
            "d2h_bytes_per_step": d2h * world, "ms_per_step": e2e_ms,
-           "note": "every step: H2D of A, this rank's B columns and bias from pinned memory, GemmEx through the "
-                   "C-ABI, D2H of C; steps pipelined over two copy streams (uploads of step i+1 overlap the GEMM "
-                   "and download of step i)"}
+           "note": "every step: H2D from pinned memory of this rank's 1/N row band of A (then one NCCL "
+                   "all-gather of A over NVLink), its B columns and bias; GemmEx through the C-ABI; D2H of its C "
+                   "columns; steps pipelined over two copy streams (uploads of step i+1 overlap the GEMM and "
+                   "download of step i)"}
     del hA, hB, hC, dA, dB, dbias, dC
     h.clear_epilogue()
+
+    attention = run_attention_sharded(args, peaks, dev, stream, rank, world, barrier, max_over_ranks)
 
     secondary = {}
     cpu = None
@@ -350,6 +366,7 @@ def run_gpu(args):
             "config": config_dict(world),
             "frac_of_peak": value / (peak * world),
             "roofline": roofline, "clocks": clk, "e2e": e2e, "gpu_launches": args.steps,
+            "attention": attention,
             "cpu_baseline": cpu, "secondary": secondary,
         }
         print(json.dumps(line), flush=True)
@@ -358,6 +375,59 @@ def run_gpu(args):
 
         dist.destroy_process_group()
     return 0
+
+
+def run_attention_sharded(args, peaks, dev, stream, rank, world, barrier, max_over_ranks):
+    """BASELINE config 4 (causal attention forward, bf16, B=8 H=32 S=4096 D=128,
+    fp32 LSE) sharded over batch x heads: every rank runs grxdnnAttentionForward
+    on its 256 / world (batch, head) pairs through shard.attention_head_parallel,
+    with no collective (each rank keeps its own heads). Device time per step is
+    the max over ranks; value = the whole job's FLOP / that time."""
+    import torch
+
+    from grxcp_b200 import dnn as D
+    from grxcp_b200 import shard
+
+    Bq, H, S, Dh = 8, 32, 4096, 128
+    g = torch.Generator(device=dev).manual_seed(99)
+    q = torch.randn(Bq, H, S, Dh, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(Bq, H, S, Dh, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(Bq, H, S, Dh, device=dev, generator=g).to(torch.bfloat16)
+    o = torch.empty_like(q)
+    lse = torch.empty(Bq, H, S, device=dev)
+    dh = D.Handle()
+    dh.set_stream(stream)
+
+    def step():
+        st = shard.attention_head_parallel(dh, q, k, v, o, 1 / math.sqrt(Dh), True, lse, rank=rank, world=world)
+        if st != 0:
+            raise RuntimeError(f"grxdnnAttentionForward status {st}")
+
+    steps = max(3, min(args.steps, 10))
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        step()
+    b.record(stream)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(a.elapsed_time(b) / steps)
+    barrier()
+    st = dh.execution_status()
+    dh.close()
+    if st != 0:
+        raise RuntimeError(f"attention kernel reported status {st}")
+    fl = 2.0 * Bq * H * S * S * Dh  # causal: half of 4 * B * H * S^2 * D
+    peak = peaks["bf16_tflops"]
+    del q, k, v, o, lse
+    torch.cuda.empty_cache()
+    return {"value": fl / ms / 1e9, "unit": "TFLOP/s", "ms": ms, "n_gpus": world, "steps": steps,
+            "frac": fl / ms / 1e9 / (peak * world), "scaling": "strong",
+            "config": f"causal, bf16, B=8 H=32 S=4096 D=128, fp32 LSE; {Bq * H // world} (batch, head) pairs per "
+                      "rank, no collective; FLOP = 2*B*H*S^2*D; max over ranks"}
 
 
 def _quantize_e4m3(x):

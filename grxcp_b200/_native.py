@@ -183,6 +183,13 @@ PROTOTYPES: dict[str, tuple] = {
     "grxblasSetWorkspace": (i32, [vp, vp, sz]),
     "grxblasGetWorkspaceSize": (sz, [vp, i32, i32, i32, i32, i32, i32, i32, i32, i32, i32]),
     "grxblasGetExecutionStatus": (i32, [vp]),
+    "grxblasShardGetUniqueId": (i32, [vp]),
+    "grxblasShardCommInit": (i32, [C.POINTER(vp), vp, i32, i32]),
+    "grxblasShardCommDestroy": (i32, [vp]),
+    "grxblasShardRange": (i32, [i32, i32, i32, C.POINTER(i32), C.POINTER(i32)]),
+    "grxblasGemmExColumnParallel": (i32, [vp, vp, i32, i32, i32, i32, i32, fp, vp, i32, i32, vp, i32, i32, fp, vp,
+                                          i32, i32, i32]),
+    "grxblasShardSynchronize": (i32, [vp, vp]),
     "grxblasGemmExNoAlloc": (i32, [vp, i32, i32, i32, i32, i32, fp, vp, i32, i32, vp, i32, i32, fp, vp, i32, i32, vp]),
     # grxdnn.h
     "grxdnnGetStatusString": (cp, [i32]),

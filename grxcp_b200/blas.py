@@ -186,3 +186,45 @@ def set_kernel_path(path: str | None) -> int:
 
 def cycle_slots_needed(m: int, n: int) -> int:
     return lib.grxblasCycleSlotsNeeded(None, m, n)
+
+
+# ------------------------------------------------------------------ column-parallel over NCCL
+
+def shard_unique_id() -> tuple[int, bytes]:
+    """grxblasShardGetUniqueId: (status, the 128-byte id rank 0 hands to the others)."""
+    buf = C.create_string_buffer(128)
+    st = lib.grxblasShardGetUniqueId(buf)
+    return st, buf.raw
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int, int]:
+    """grxblasShardRange: (status, start, count)."""
+    s, c = C.c_int(0), C.c_int(0)
+    st = lib.grxblasShardRange(n, rank, world, C.byref(s), C.byref(c))
+    return st, s.value, c.value
+
+
+class ShardComm:
+    """One rank's NCCL communicator for grxblasGemmExColumnParallel (current device)."""
+
+    def __init__(self, uid: bytes, rank: int, world: int):
+        self.c = C.c_void_p()
+        self.rank, self.world = rank, world
+        idbuf = C.create_string_buffer(uid, 128)
+        self.status = lib.grxblasShardCommInit(C.byref(self.c), idbuf, rank, world)
+
+    def destroy(self) -> int:
+        st = N.SUCCESS
+        if self.c:
+            st = lib.grxblasShardCommDestroy(self.c)
+            self.c = C.c_void_p()
+        return st
+
+    def gemm_ex_column_parallel(self, handle: "Handle", transa, transb, m, n, k, alpha, A, Atype, lda, B, Btype, ldb,
+                                beta, C_, Ctype, ldc, replicate: bool) -> int:
+        return lib.grxblasGemmExColumnParallel(handle.h, self.c, transa, transb, m, n, k, _fptr(alpha), ptr(A), Atype,
+                                               lda, ptr(B), Btype, ldb, _fptr(beta), ptr(C_), Ctype, ldc,
+                                               1 if replicate else 0)
+
+    def synchronize(self, handle: "Handle") -> int:
+        return lib.grxblasShardSynchronize(handle.h, self.c)

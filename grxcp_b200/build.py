@@ -38,6 +38,7 @@ SOURCES = [
     "softmax.cu",
     "conv.cu",
     "profile.cpp",
+    "shard.cpp",
 ]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

@@ -61,6 +61,7 @@ grxblasStatus_t from_cuda(cudaError_t e) {
 // configured path (call, then $GRXBLAS_KERNEL_PATH) must name the file the
 // kernels live in -- this library -- or its directory; no fallback past it.
 bool kernel_path_ok() {
+  if (grx::fault_injected("module")) return false;
   std::string cfg;
   {
     std::lock_guard<std::mutex> lock(g_path_mutex);
@@ -101,6 +102,7 @@ void* workspace(grxblasContext& ctx, size_t bytes) {
   if (bytes == 0) return nullptr;
   if (ctx.ws_user && ctx.ws_user_bytes >= bytes) return ctx.ws_user;
   if (ctx.ws_own_bytes >= bytes) return ctx.ws_own;
+  if (grx::fault_injected("alloc")) return nullptr;
   if (ctx.ws_own) cudaFreeAsync(ctx.ws_own, ctx.stream);
   ctx.ws_own = nullptr;
   ctx.ws_own_bytes = 0;
@@ -183,7 +185,7 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
                              int n, int k, const float* alpha, const void* A, grxDataType_t Atype, int lda,
                              long long strideA, const void* B, grxDataType_t Btype, int ldb, long long strideB,
                              const float* beta, void* C, grxDataType_t Ctype, int ldc, long long strideC,
-                             int batch) {
+                             int batch, long long col0 = 0) {
   // Order and codes: reference grxblas.cpp:506-524 (GemmEx) and :882-897
   // (the batch rules of sgemm_batched).
   if (!handle) return GRXBLAS_STATUS_NOT_INITIALIZED;
@@ -216,7 +218,13 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
     if (ctx.has_epi && (ctx.epi.bias || ctx.epi.scaleMode != GRXBLAS_SCALE_NONE))
       return GRXBLAS_STATUS_NOT_SUPPORTED;
   }
-  const grxblasEpilogue_t epi = ctx.has_epi ? ctx.epi : grxblasEpilogue_t{};
+  grxblasEpilogue_t epi = ctx.has_epi ? ctx.epi : grxblasEpilogue_t{};
+  if (col0 != 0) {
+    // columns [col0, col0 + n) of a wider problem: per-column bias and scales start at col0
+    if (epi.bias && !epi.biasOverRows)
+      epi.bias = static_cast<const char*>(epi.bias) + col0 * (epi.biasType == GRX_R_16BF ? 2 : 4);
+    if (epi.scaleMode == GRXBLAS_SCALE_ROWCOL && epi.scaleB) epi.scaleB += col0;
+  }
   if (epi.scaleMode != GRXBLAS_SCALE_NONE && (!epi.scaleA || !epi.scaleB)) return GRXBLAS_STATUS_INVALID_VALUE;
   if ((unsigned)epi.scaleMode > 2u) return GRXBLAS_STATUS_INVALID_VALUE;
   if (epi.bias && epi.biasType != GRX_R_32F && epi.biasType != GRX_R_16BF) return GRXBLAS_STATUS_NOT_SUPPORTED;
@@ -316,6 +324,16 @@ grxblasStatus_t gemm_ex_impl(grxblasHandle_t handle, grxblasOperation_t transa, 
 }
 
 }  // namespace
+
+namespace grx {
+grxblasStatus_t gemm_ex_columns(grxblasHandle_t handle, grxblasOperation_t transa, grxblasOperation_t transb, int m,
+                                int n, int k, const float* alpha, const void* A, grxDataType_t Atype, int lda,
+                                const void* B, grxDataType_t Btype, int ldb, const float* beta, void* C,
+                                grxDataType_t Ctype, int ldc, long long col0) {
+  return gemm_ex_impl(handle, transa, transb, m, n, k, alpha, A, Atype, lda, 0, B, Btype, ldb, 0, beta, C, Ctype, ldc,
+                      0, 1, col0);
+}
+}  // namespace grx
 
 extern "C" {
 

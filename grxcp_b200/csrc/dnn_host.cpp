@@ -80,6 +80,7 @@ grxdnnStatus_t check_norm(grxdnnHandle_t h, int rows, int hidden, const void* x,
 void* workspace(grxdnnContext& ctx, size_t bytes) {
   std::lock_guard<std::mutex> lock(ctx.mutex);
   if (ctx.ws_bytes >= bytes) return ctx.ws;
+  if (grx::fault_injected("alloc")) return nullptr;
   if (ctx.ws) cudaFreeAsync(ctx.ws, ctx.stream);
   ctx.ws = nullptr;
   ctx.ws_bytes = 0;

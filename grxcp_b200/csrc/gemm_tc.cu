@@ -571,11 +571,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
-      if (!ok) {
-        // Let every armed stage land before the CTA's shared memory goes away.
-        for (int s = 0; s < kStages; ++s)
-          if (issued_mask & (1u << s)) wait_drain(&full[s], (issued_par >> s) & 1u, p.timeout_ns, p.err_word);
-      }
+      // Let every armed stage land before the CTA's shared memory goes away:
+      // after an abort elsewhere in the CTA (the MMA issuer stops consuming)
+      // the last loads may still be in flight even though this loop finished.
+      // On a normal exit every stage's last phase has completed already.
+      for (int s = 0; s < kStages; ++s)
+        if (issued_mask & (1u << s)) wait_drain(&full[s], (issued_par >> s) & 1u, p.timeout_ns, p.err_word);
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -815,9 +816,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       // Both CTAs' loads complete on the leader's full barriers: after an
       // abort the leader lets every armed stage land; the closing cluster
       // barrier holds the peer until then.
-      if (!ok && leader) {
+      if (leader) {
         for (int s = 0; s < kPairStages; ++s)
           if (armed & (1u << s)) wait_drain(&full[s], (armed_par >> s) & 1u, p.timeout_ns, p.err_word);
+      }
+      // After an abort the peer CTA may have issued loads (completing on the
+      // leader's barriers) for stages the leader never armed; give copies in
+      // flight time to land before either CTA's shared memory is released.
+      if (*abort_flag) {
+        const uint64_t t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 50000ull) {
+        }
       }
     }
   } else if (warp == 1) {

@@ -12,6 +12,20 @@
 
 namespace grx {
 
+bool fault_injected(const char* site) {
+  const char* e = getenv("GRX_FAULT_INJECT");
+  if (!e || !*e) return false;
+  const size_t n = strlen(site);
+  for (const char* p = e; *p;) {
+    const char* end = strchr(p, ',');
+    const size_t len = end ? (size_t)(end - p) : strlen(p);
+    if (len == n && strncmp(p, site, n) == 0) return true;
+    if (!end) break;
+    p = end + 1;
+  }
+  return false;
+}
+
 int ensure_device(DeviceState& d) {
   if (d.device >= 0) return 0;
   int dev = -1;
@@ -25,6 +39,7 @@ int ensure_device(DeviceState& d) {
     return 1;
   }
   int* w = nullptr;
+  if (fault_injected("alloc")) return 2;
   if (cudaMalloc(&w, sizeof(int)) != cudaSuccess) {
     cudaGetLastError();
     return 2;

@@ -33,4 +33,15 @@ const char* library_path();
 // True when `path` names this library file or the directory holding it.
 bool path_names_library(const char* path);
 
+// Host-side fault injection. GRX_FAULT_INJECT holds a comma-separated list of
+// sites whose next call this library treats as failed, read on every check:
+//   alloc      every device allocation the library makes (error word,
+//              workspace): the API returns ALLOC_FAILED
+//   module     kernel-path resolution (GRXBLAS_KERNEL_PATH rule): the API
+//              returns NOT_INITIALIZED, as when the kernels are not found
+//   nccl_init  communicator creation in grxblasShardCommInit: EXECUTION_FAILED
+//   nccl_load  loading libnccl: NOT_SUPPORTED
+// Nothing is injected on the device: no kernel is made to fault or hang.
+bool fault_injected(const char* site);
+
 }  // namespace grx

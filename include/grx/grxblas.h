@@ -233,6 +233,53 @@ size_t          grxblasGetWorkspaceSize(grxblasHandle_t handle, grxblasOperation
  * (EXECUTION_FAILED), or whether the stream reported an error. Clears the flag. */
 grxblasStatus_t grxblasGetExecutionStatus(grxblasHandle_t handle);
 
+/* Additive (no counterpart in the reference, which runs on one device):
+ * column-parallel GemmEx across GPUs, one process per GPU, over NCCL.
+ *
+ *   rank 0:       grxblasShardGetUniqueId(&id); send id to the other ranks
+ *   every rank:   grxblasShardCommInit(&comm, &id, rank, world)   (current device)
+ *                 grxblasGemmExColumnParallel(handle, comm, ..., replicate)
+ *                 grxblasShardSynchronize(handle, comm)
+ *                 grxblasShardCommDestroy(comm)
+ *
+ * grxblasGemmExColumnParallel takes the arguments of grxblasGemmEx for the
+ * WHOLE problem (B and C are the full n-column operands; A is replicated) and
+ * computes this rank's columns grxblasShardRange(n, rank, world) with one local
+ * GemmEx on the handle's stream; the handle's epilogue applies, with per-column
+ * bias and scales read at the same global columns. replicate != 0 then
+ * broadcasts every rank's column block of C (its ld padding rows included) so
+ * that C is complete on every rank; replicate == 0 leaves each rank its own
+ * columns only. Calls return after enqueueing; every rank must make the same
+ * calls in the same order.
+ *
+ * Failures are detected on the host: the communicator is non-blocking, and
+ * initialisation, each enqueue and grxblasShardSynchronize give up after
+ * GRX_SHARD_TIMEOUT_MS (default 60000 ms; a rank that never joined or has
+ * left), abort the communicator and return EXECUTION_FAILED. An aborted
+ * communicator refuses further calls with EXECUTION_FAILED and must be
+ * destroyed. NOT_SUPPORTED: libnccl.so.2 could not be loaded. */
+typedef struct {
+  char internal[128];
+} grxblasShardUniqueId_t;
+typedef struct grxblasShardContext* grxblasShardComm_t;
+
+grxblasStatus_t grxblasShardGetUniqueId(grxblasShardUniqueId_t* id);
+grxblasStatus_t grxblasShardCommInit(grxblasShardComm_t* comm, const grxblasShardUniqueId_t* id,
+                                     int rank, int world);
+grxblasStatus_t grxblasShardCommDestroy(grxblasShardComm_t comm);
+/* Contiguous split of n columns: the first n % world ranks get one more. */
+grxblasStatus_t grxblasShardRange(int n, int rank, int world, int* start, int* count);
+grxblasStatus_t grxblasGemmExColumnParallel(grxblasHandle_t handle, grxblasShardComm_t comm,
+                                            grxblasOperation_t transa, grxblasOperation_t transb,
+                                            int m, int n, int k, const float* alpha,
+                                            const void* A, grxDataType_t Atype, int lda,
+                                            const void* B, grxDataType_t Btype, int ldb,
+                                            const float* beta,
+                                            void* C, grxDataType_t Ctype, int ldc, int replicate);
+/* Waits (bounded, as above) for the handle's stream, including the broadcasts,
+ * then reports grxblasGetExecutionStatus. */
+grxblasStatus_t grxblasShardSynchronize(grxblasHandle_t handle, grxblasShardComm_t comm);
+
 /* No counterpart in the reference. grxblasGemmEx for callers that may not
  * allocate device memory -- code whose device memory is owned by another
  * allocator (framework plug-ins, fixed-budget serving processes) or that must
