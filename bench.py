@@ -255,10 +255,10 @@ def run_gpu(args):
             parts = line.split()
             if len(parts) == 2 and parts[0] == "gemm_bf16_8192_per_launch_bytes":
                 traffic = float(parts[1]) * nl / N  # scales with the column shard
-    # the library's choice (gemm_tc.cu use_pair): CTA pairs for 16-bit problems with at least four
-    # 256 x 256 pair-tiles per pair of SMs
+    # the library's choice (gemm_tc.cu use_pair): CTA pairs for 16-bit problems with at least one
+    # 256 x 256 pair-tile per pair of SMs
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    pair = M >= 256 and nl >= 256 and -(-M // 256) * -(-nl // 256) >= 4 * (sms // 2)
+    pair = M >= 256 and nl >= 256 and -(-M // 256) * -(-nl // 256) >= sms // 2
     kernel_name = "grx::tc_gemm_pair_kernel<kind::f16, bf16 out>" if pair else "grx::tc_gemm_kernel<kind::f16, bf16 out>"
     roofline = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "traffic": traffic, "peak_source": f"{peaks_src} bf16_tflops (burst)",

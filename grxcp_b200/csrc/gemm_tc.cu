@@ -994,17 +994,20 @@ static cudaError_t launch_pair_impl(const CUtensorMap& ma, const CUtensorMap& mb
 // Measured on B200 (8192^3): the pair kernel wins for 16-bit operands with an
 // MN-major operand (NN +8 %, NT +14 %, TT +2 %) and ties on TN; it loses for
 // 8-bit operands (the tensor pipe consumes k twice as fast there, so the
-// extra cross-CTA hand-off shows) and for problems with fewer than ~4 tiles
-// per CTA pair. GRX_GEMM_NO_PAIR=1 forces the single-CTA kernel;
-// GRX_GEMM_FORCE_PAIR=1 takes the pair kernel for every type whenever m and n
-// are at least 256 (the tests use it to cover that kernel at modest sizes).
+// extra cross-CTA hand-off shows). With bf16 data of the bench's scale it
+// also wins on the column-parallel slices once there is at least one pair
+// tile per SM pair: 8192 x 2048 x 8192 215 vs 222 us, 8192 x 1024 x 8192 109
+// vs 114 us, 18944 x 256 x 8192 (one round) 66 vs 73 us.
+// GRX_GEMM_NO_PAIR=1 forces the single-CTA kernel; GRX_GEMM_FORCE_PAIR=1
+// takes the pair kernel for every type whenever m and n are at least 256 (the
+// tests use it to cover that kernel at modest sizes).
 static bool use_pair(int kind, const TcGemmParams& p, int num_sms) {
   if (getenv("GRX_GEMM_NO_PAIR")) return false;
   if (getenv("GRX_GEMM_FORCE_PAIR")) return p.m >= kPairTileM && p.n >= kPairTileN;
   if (kind != kKindF16) return false;
   const long long tiles = (long long)((p.m + kPairTileM - 1) / kPairTileM) * ((p.n + kPairTileN - 1) / kPairTileN) *
                           p.batch;
-  return p.m >= kPairTileM && p.n >= kPairTileN && tiles >= 4LL * (num_sms / 2);
+  return p.m >= kPairTileM && p.n >= kPairTileN && tiles >= (long long)(num_sms / 2);
 }
 
 // Split-K plan for the last, partial wave of the single-CTA kernel. A
