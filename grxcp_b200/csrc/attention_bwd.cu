@@ -16,7 +16,11 @@
 //       in TMEM. It recomputes S and dP instead of sharing dS with the KV
 //       kernel through fp32 atomics.
 // CTA: 320 threads. Warp 0 is the TMA producer (one thread): the resident pair
-// once, then the streamed pair of each block through a 2-stage ring. Warp 1 is
+// once, then the streamed pair of each block half by half through a 4-stage
+// ring of half-blocks (64 rows of both streamed tensors, 32 KiB): a stage is
+// released as soon as that half's gradient MMAs are done, so the loads of the
+// next block overlap a whole block of work (with whole-block stages of the same
+// 128 KiB the MMA issuer waited ~2000 cycles per block for its next tile). Warp 1 is
 // the MMA issuer (one thread). Warps 2..9 (two per TMEM lane quadrant) form P
 // and dS. Each streamed block is worked in two halves of 64 (queries for the
 // KV kernel, keys for the Q kernel) that ping-pong: while the compute warps
@@ -44,6 +48,7 @@
 #include "profile.h"
 #include "ptx.cuh"
 
+
 namespace grx {
 
 namespace {
@@ -52,11 +57,13 @@ constexpr int kD = 128;
 constexpr int kB = 128;                   // queries or keys per block
 constexpr int kTile = kB * kD * 2;        // 32 KiB bf16 tile (two 16 KiB swizzle halves)
 constexpr int kHalf = 16384;
+constexpr int kHS = 32768;                // half-block stage: 64 rows of each streamed tensor
+constexpr int kRing = 4;                  // half-block stages
 constexpr int kThreads = 320;
 constexpr int kComputeWarps = 8;  // two per TMEM lane quadrant, one per 64-column half
 constexpr int kModeKV = 0, kModeQ = 1;
-// Resident pair (K,V or Q,dO) and a 2-stage ring of streamed pairs.
-constexpr int kSmem = 2 * kTile + 2 * 2 * kTile + 1024 + 256;
+// Resident pair (K,V or Q,dO) and the ring of streamed half-blocks.
+constexpr int kSmem = 2 * kTile + kRing * kHS + 1024 + 256;
 constexpr float kLog2e = 1.4426950408889634f;
 // Share of exponentials moved to the FMA pipe (every n-th pair; 0 = none). Measured at config 4:
 // none 4.66 ms, 1/8 4.80, 1/4 4.93, 1/2 5.11 -- this stage is FMA-issue bound, not SFU bound.
@@ -91,10 +98,15 @@ __device__ __noinline__ void drain_wait(uint64_t* bar, uint32_t parity, uint64_t
 __device__ __forceinline__ uint64_t kmajor(uint32_t base, int kk) {
   return sw128_desc(base + (kk >> 2) * kHalf + (kk & 3) * 32, 16, 1024);
 }
-// The same tile read MN-major (its rows are the k index): kk selects 16 rows;
-// the two 64-column halves are the two MN atoms, kHalf apart.
-__device__ __forceinline__ uint64_t mnmajor(uint32_t base, int kk) {
-  return sw128_desc(base + kk * 2048, kHalf, 1024);
+// A half-block stage holds, per streamed tensor, 64 rows x 128 bf16 as two
+// 64-element swizzle halves of 8 KiB. K-major read (rows = N of the scores):
+__device__ __forceinline__ uint64_t kmajor_h(uint32_t base, int kk) {
+  return sw128_desc(base + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+}
+// The same 64 rows read MN-major (rows = the k index): kk selects 16 rows; the
+// two 64-column halves are the two MN atoms, 8 KiB apart.
+__device__ __forceinline__ uint64_t mnmajor_h(uint32_t base, int kk) {
+  return sw128_desc(base + kk * 2048, 8192, 1024);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -172,16 +184,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
   uint8_t* sRes = smem;               // KV: K, V.  Q: Q, dO.
-  uint8_t* sRing = sRes + 2 * kTile;  // stage s: pair at s * 2 * kTile (KV: Q, dO.  Q: K, V)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + 4 * kTile);
+  // stage u % kRing of half-block u = 2 t + h: rows [64 h, 64 h + 64) of the
+  // streamed pair (KV: Q, dO.  Q: K, V), first tensor at 0, second at 16 KiB.
+  uint8_t* sRing = sRes + 2 * kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRing + kRing * kHS);
   uint64_t* res_full = bars;
-  uint64_t* ring_full = bars + 1;   // [2]
-  uint64_t* ring_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;      // [2] scores of half h in TMEM
-  uint64_t* p_full = bars + 7;      // [2] half h's P / dS written back to TMEM (8 warps)
-  uint64_t* acc_done = bars + 9;
-  uint64_t* drain = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* ring_full = bars + 1;              // [kRing]
+  uint64_t* ring_empty = bars + 1 + kRing;     // [kRing]
+  uint64_t* s_full = bars + 1 + 2 * kRing;     // [2] scores of half h in TMEM
+  uint64_t* p_full = bars + 3 + 2 * kRing;     // [2] half h's P / dS written back to TMEM (8 warps)
+  uint64_t* acc_done = bars + 5 + 2 * kRing;
+  uint64_t* drain = bars + 6 + 2 * kRing;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7 + 2 * kRing);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // KV kernel: per compute warp, its 32 columns' (-LSE log2 e, Delta) pairs.
   __shared__ __align__(16) float2 col_stats[kComputeWarps][32];
@@ -202,9 +216,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(res_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kRing; ++s) {
       mbar_init(&ring_full[s], 1);
       mbar_init(&ring_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], kComputeWarps);
     }
@@ -241,26 +257,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint32_t armed = 0, armed_par = 0;
       bool ok = true;
-      for (int t = 0; t < n_it; ++t) {
-        const int st = t & 1;
-        const uint32_t ph = (t >> 1) & 1;
+      for (int u = 0; u < 2 * n_it; ++u) {
+        const int st = u % kRing;
+        const uint32_t ph = (uint32_t)(u / kRing) & 1u;
         if (!wait_bounded(&ring_empty[st], ph ^ 1u, wc, kErrTimeoutProducer)) {
           ok = false;
           break;
         }
-        const int blk = it0 + t;
-        uint8_t* dst = sRing + st * 2 * kTile;
-        mbar_arrive_expect_tx(&ring_full[st], 2 * kTile);
+        const int row0 = (it0 + (u >> 1)) * kB + (u & 1) * 64;
+        uint8_t* dst = sRing + st * kHS;
+        mbar_arrive_expect_tx(&ring_full[st], kHS);
         for (int h = 0; h < 2; ++h) {
-          tma_load_4d(dst + h * kHalf, s0, &ring_full[st], h * 64, blk * kB, hi, bi);
-          tma_load_4d(dst + kTile + h * kHalf, s1, &ring_full[st], h * 64, blk * kB, hi, bi);
+          tma_load_4d(dst + h * 8192, s0, &ring_full[st], h * 64, row0, hi, bi);
+          tma_load_4d(dst + 16384 + h * 8192, s1, &ring_full[st], h * 64, row0, hi, bi);
         }
         armed |= 1u << st;
         armed_par = (armed_par & ~(1u << st)) | (ph << st);
       }
       drain_wait(res_full, 0, p.timeout_ns, p.err_word);
       if (!ok)
-        for (int s = 0; s < 2; ++s)
+        for (int s = 0; s < kRing; ++s)
           if (armed & (1u << s)) drain_wait(&ring_full[s], (armed_par >> s) & 1u, p.timeout_ns, p.err_word);
     }
   } else if (warp == 1) {
@@ -269,26 +285,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_s = make_idesc(1, 1, 1, 0, 0, 128, 64);   // scores of a half: N = 64
       constexpr uint32_t idesc_g = make_idesc(1, 1, 1, 0, 1, 128, 128);  // A from TMEM, B MN-major, N = 128
       const uint32_t res = smem_u32(sRes), ring = smem_u32(sRing);
-      // Per half h of streamed block t: scores (A resident, K-major; B the
-      // streamed tile's rows [64 h, 64 h + 64), K-major) and dP likewise.
+      auto stage = [&](int u) { return ring + (uint32_t)((u % kRing) * kHS); };
+      auto landed = [&](int u) {
+        return wait_bounded(&ring_full[u % kRing], (uint32_t)(u / kRing) & 1u, wc, kErrTimeoutMma);
+      };
+      // Half h of streamed block t: scores (A resident, K-major; B the half's
+      // 64 streamed rows, K-major) and dP likewise.
       auto scores = [&](int t, int h) {
-        const uint32_t st = ring + (t & 1) * 2 * kTile + h * 8192;
+        const uint32_t st = stage(2 * t + h);
         const uint32_t d_s = tmem + s_base + 128 * h;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) mma_ss<0>(d_s, kmajor(res, kk), kmajor(st, kk), idesc_s, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) mma_ss<0>(d_s, kmajor(res, kk), kmajor_h(st, kk), idesc_s, kk > 0 ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_ss<0>(d_s + 64, kmajor(res + kTile, kk), kmajor(st + kTile, kk), idesc_s, kk > 0 ? 1u : 0u);
+          mma_ss<0>(d_s + 64, kmajor(res + kTile, kk), kmajor_h(st + 16384, kk), idesc_s, kk > 0 ? 1u : 0u);
         mma_commit(&s_full[h]);
       };
-      bool ok = wait_bounded(res_full, 0, wc, kErrTimeoutMma) && wait_bounded(&ring_full[0], 0, wc, kErrTimeoutMma);
+      bool ok = wait_bounded(res_full, 0, wc, kErrTimeoutMma) && landed(0);
       if (ok) {
         tc_fence_after();
         scores(0, 0);
-        scores(0, 1);
+        ok = landed(1);
+        if (ok) {
+          tc_fence_after();
+          scores(0, 1);
+        }
       }
       for (int t = 0; t < n_it && ok; ++t) {
-        const uint32_t st = ring + (t & 1) * 2 * kTile;
         for (int h = 0; h < 2 && ok; ++h) {
           if (!wait_bounded(&p_full[h], t & 1, wc, kErrTimeoutMma)) {
             ok = false;
@@ -296,23 +319,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t sh = tmem + s_base + 128 * h;
+          const uint32_t st = stage(2 * t + h);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t acc = (t > 0 || h > 0 || kk > 0) ? 1u : 0u;
             if (MODE == kModeKV) {
               // dV += P^T dO_h, dK += dS^T Q_h (M = keys, K = this half's 64 queries)
-              mma_ts_f16(tmem, sh + half_col(kk), mnmajor(st + kTile + h * 8192, kk), idesc_g, acc);
-              mma_ts_f16(tmem + 128, sh + 64 + half_col(kk), mnmajor(st + h * 8192, kk), idesc_g, acc);
+              mma_ts_f16(tmem, sh + half_col(kk), mnmajor_h(st + 16384, kk), idesc_g, acc);
+              mma_ts_f16(tmem + 128, sh + 64 + half_col(kk), mnmajor_h(st, kk), idesc_g, acc);
             } else {
               // dQ += dS_h K_h (M = queries, K = this half's 64 keys)
-              mma_ts_f16(tmem, sh + half_col(kk), mnmajor(st + h * 8192, kk), idesc_g, acc);
+              mma_ts_f16(tmem, sh + half_col(kk), mnmajor_h(st, kk), idesc_g, acc);
             }
           }
-          if (h == 1) mma_commit(&ring_empty[t & 1]);
+          mma_commit(&ring_empty[(2 * t + h) % kRing]);
           if (t + 1 < n_it) {
             // In-order execution: the next scores land after the MMAs above
             // have read this half's columns.
-            if (h == 0 && !wait_bounded(&ring_full[(t + 1) & 1], ((t + 1) >> 1) & 1, wc, kErrTimeoutMma)) {
+            if (!landed(2 * (t + 1) + h)) {
               ok = false;
               break;
             }
@@ -499,11 +523,12 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// [batch, heads, seq, 128] bf16 -> 4-D map {128, seq, heads, batch}, box {64, 128, 1, 1}.
+// [batch, heads, seq, 128] bf16 -> 4-D map {128, seq, heads, batch}, box {64, box_rows, 1, 1}
+// (128 rows for a resident tile, 64 for a streamed half-block).
 // A batch or head stride of 0 (broadcast) is replaced by the dense stride the
 // map needs for a dimension of extent 1.
 bool make_map(CUtensorMap* m, const void* base, int batch, int heads, int seq, long long sb, long long sh,
-              long long ss) {
+              long long ss, int box_rows) {
   if (batch == 1) sb = (long long)heads * sh;
   if (heads == 1) sh = (long long)seq * ss;
   if (sb == 0) sb = 8;
@@ -514,7 +539,7 @@ bool make_map(CUtensorMap* m, const void* base, int batch, int heads, int seq, l
   if (!enc) return false;
   cuuint64_t dims[4] = {(cuuint64_t)kD, (cuuint64_t)seq, (cuuint64_t)heads, (cuuint64_t)batch};
   cuuint64_t strides[3] = {(cuuint64_t)(ss * 2), (cuuint64_t)(sh * 2), (cuuint64_t)(sb * 2)};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   return enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -545,12 +570,17 @@ size_t attention_bwd_workspace_bytes(const AttnBwdArgs& a) {
 
 cudaError_t launch_attention_bwd(const AttnBwdArgs& a, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (!ws || ws_bytes < attention_bwd_workspace_bytes(a)) return cudaErrorInvalidValue;
-  CUtensorMap mq, mk, mv, md;
-  if (!make_map(&mq, a.q, a.batch, a.heads, a.seq_q, a.q_sb, a.q_sh, a.q_ss) ||
-      !make_map(&mk, a.k, a.batch, a.heads, a.seq_k, a.k_sb, a.k_sh, a.k_ss) ||
-      !make_map(&mv, a.v, a.batch, a.heads, a.seq_k, a.v_sb, a.v_sh, a.v_ss) ||
-      !make_map(&md, a.dout, a.batch, a.heads, a.seq_q, a.do_sb, a.do_sh, a.do_ss))
-    return cudaErrorNotSupported;
+  // Resident tiles (KV kernel: K, V; Q kernel: Q, dO) are loaded as 128-row
+  // boxes, streamed half-blocks as 64-row boxes.
+  CUtensorMap mq[2], mk[2], mv[2], md[2];  // [0]: 128-row boxes, [1]: 64-row boxes
+  for (int i = 0; i < 2; ++i) {
+    const int rows = i == 0 ? 128 : 64;
+    if (!make_map(&mq[i], a.q, a.batch, a.heads, a.seq_q, a.q_sb, a.q_sh, a.q_ss, rows) ||
+        !make_map(&mk[i], a.k, a.batch, a.heads, a.seq_k, a.k_sb, a.k_sh, a.k_ss, rows) ||
+        !make_map(&mv[i], a.v, a.batch, a.heads, a.seq_k, a.v_sb, a.v_sh, a.v_ss, rows) ||
+        !make_map(&md[i], a.dout, a.batch, a.heads, a.seq_q, a.do_sb, a.do_sh, a.do_ss, rows))
+      return cudaErrorNotSupported;
+  }
   const void* outs[3] = {a.dq, a.dk, a.dv};
   const long long oss[3] = {a.dq_ss, a.dk_ss, a.dv_ss};
   for (int i = 0; i < 3; ++i)
@@ -588,12 +618,12 @@ cudaError_t launch_attention_bwd(const AttnBwdArgs& a, void* ws, size_t ws_bytes
   p.o0_sb = a.dk_sb; p.o0_sh = a.dk_sh; p.o0_ss = a.dk_ss;
   p.out1 = a.dv;
   p.o1_sb = a.dv_sb; p.o1_sh = a.dv_sh; p.o1_ss = a.dv_ss;
-  cudaError_t e = launch_mode<kModeKV>(mq, mk, mv, md, p, s);
+  cudaError_t e = launch_mode<kModeKV>(mq[1], mk[0], mv[0], md[1], p, s);
   if (e != cudaSuccess) return e;
   p.out0 = a.dq;
   p.o0_sb = a.dq_sb; p.o0_sh = a.dq_sh; p.o0_ss = a.dq_ss;
   p.out1 = nullptr;
-  return launch_mode<kModeQ>(mq, mk, mv, md, p, s);
+  return launch_mode<kModeQ>(mq[0], mk[1], mv[1], md[0], p, s);
 }
 
 }  // namespace grx
