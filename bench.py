@@ -248,13 +248,15 @@ def run_gpu(args):
     per_launch_flops = 2.0 * M * nl * K
     achieved = per_launch_flops / (ms_local * 1e-3) / 1e12
     peak = peaks["bf16_tflops"]
+    # DRAM bytes of one launch of this rank's slice, from an ncu capture of that
+    # exact shape (bench.py --profile gemm --profile-cols nl); null when absent.
     traffic = None
     tr = ROOT / "profiles" / "traffic.txt"
     if tr.exists():
         for line in tr.read_text().splitlines():
             parts = line.split()
-            if len(parts) == 2 and parts[0] == "gemm_bf16_8192_per_launch_bytes":
-                traffic = float(parts[1]) * nl / N  # scales with the column shard
+            if len(parts) == 2 and parts[0] == f"gemm_bf16_{M}x{nl}x{K}_per_launch_bytes":
+                traffic = float(parts[1])
     # the library's choice (gemm_tc.cu use_pair): CTA pairs for 16-bit problems with at least one
     # 256 x 256 pair-tile per pair of SMs
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -430,6 +432,28 @@ def run_attention_sharded(args, peaks, dev, stream, rank, world, barrier, max_ov
                       "rank, no collective; FLOP = 2*B*H*S^2*D; max over ranks"}
 
 
+def measure_8bit_peaks(dev, stream):
+    """Roofline denominators for the 8-bit kinds, measured on this GPU the way
+    the bf16 peak is: a vendor-library dense GEMM at 8192^3, timed with CUDA
+    events (e4m3 via torch._scaled_mm, int8 via torch._int_mm). Returns
+    (fp8 TFLOP/s, int8 TOP/s)."""
+    import torch
+
+    n = 8192
+    g = torch.Generator(device=dev).manual_seed(5)
+    a = torch.randn(n, n, device=dev, generator=g).div(8).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, device=dev, generator=g).div(8).to(torch.float8_e4m3fn).t()  # column-major
+    one = torch.ones((), device=dev)
+    ms8 = _time(lambda: torch._scaled_mm(a, b, scale_a=one, scale_b=one, out_dtype=torch.bfloat16), 10, stream)
+    ia = torch.randint(-128, 128, (n, n), device=dev, dtype=torch.int8, generator=g)
+    ib = torch.randint(-128, 128, (n, n), device=dev, dtype=torch.int8, generator=g).t()
+    msi = _time(lambda: torch._int_mm(ia, ib), 10, stream)
+    del a, b, ia, ib
+    torch.cuda.empty_cache()
+    fl = 2.0 * n ** 3
+    return fl / ms8 / 1e9, fl / msi / 1e9
+
+
 def _quantize_e4m3(x):
     """[batch, rows, k] fp32 -> e4m3 codes and one scale (amax / 448) per batch member."""
     import torch
@@ -540,10 +564,10 @@ def run_secondary(args, peaks, dev, stream):
     ms = _time(lambda: bh.gemm_strided_batched_ex(Nn.OP_T, Nn.OP_N, m5, n5, k5, 1.0, a8, Nn.GRX_R_8F_E4M3, k5,
                                                   m5 * k5, b8, Nn.GRX_R_8F_E4M3, k5, n5 * k5, 0.0, c5,
                                                   Nn.GRX_R_16BF, m5, m5 * n5, bt), 5, stream)
-    fp8_peak = 2 * bf16_peak
+    fp8_peak, i8_peak = measure_8bit_peaks(dev, stream)
     out["fp8_batched_gemm"] = {"value": fl5 / ms / 1e9, "unit": "TFLOP/s", "ms": ms,
-                               "frac": fl5 / ms / 1e9 / fp8_peak,
-                               "peak_note": "fp8 peak taken as 2x the measured bf16 peak",
+                               "frac": fl5 / ms / 1e9 / fp8_peak, "peak": fp8_peak,
+                               "peak_note": "measured here: cuBLASLt e4m3 GEMM 8192^3 (torch._scaled_mm), burst",
                                "config": "e4m3, batch 16, 4096x14336x4096, per-tensor scales, bf16 out"}
     # int8 variant with per-row / per-column scales
     # int8 codes with per-row (A) / per-column (B) scales amax / 127
@@ -554,7 +578,9 @@ def run_secondary(args, peaks, dev, stream):
                                                   m5 * k5, i8b, Nn.GRX_R_8I, k5, n5 * k5, 0.0, c5,
                                                   Nn.GRX_R_16BF, m5, m5 * n5, bt), 5, stream)
     out["int8_rowcol_batched_gemm"] = {"value": fl5 / ms / 1e9, "unit": "TOP/s", "ms": ms,
-                                       "frac": fl5 / ms / 1e9 / fp8_peak,
+                                       "frac": fl5 / ms / 1e9 / i8_peak, "peak": i8_peak,
+                                       "peak_note": "measured here: cuBLASLt int8 GEMM 8192^3 -> int32 "
+                                                    "(torch._int_mm), burst",
                                        "config": "int8, batch 16, 4096x14336x4096, per-row/col scales, bf16 out"}
     bh.clear_epilogue()
     del a8, b8, i8a, i8b, c5
@@ -594,12 +620,13 @@ def run_profile(args):
         h = B.Handle()
         if args.profile == "gemm":
             A = (torch.randn(M, K, device=dev, generator=g) / math.sqrt(K)).to(torch.bfloat16)
-            Bm = (torch.randn(N, K, device=dev, generator=g) / math.sqrt(K)).to(torch.bfloat16)
-            C = torch.empty(N, M, device=dev, dtype=torch.bfloat16)
-            bias = torch.randn(N, device=dev, generator=g) * 0.02
+            nc = args.profile_cols or N  # one rank's column slice of the N-GPU run (N / world)
+            Bm = (torch.randn(nc, K, device=dev, generator=g) / math.sqrt(K)).to(torch.bfloat16)
+            C = torch.empty(nc, M, device=dev, dtype=torch.bfloat16)
+            bias = torch.randn(nc, device=dev, generator=g) * 0.02
             h.set_epilogue(bias=bias, bias_type=Nn.GRX_R_32F)
             for _ in range(n_iter):
-                B.check(h.gemm_ex(1, 0, M, N, K, 1.0, A, Nn.GRX_R_16BF, K, Bm, Nn.GRX_R_16BF, K, 0.0, C,
+                B.check(h.gemm_ex(1, 0, M, nc, K, 1.0, A, Nn.GRX_R_16BF, K, Bm, Nn.GRX_R_16BF, K, 0.0, C,
                                   Nn.GRX_R_16BF, M))
         else:
             bt, m5, n5, k5 = 16, 4096, 14336, 4096
@@ -671,6 +698,8 @@ def main():
     ap.add_argument("--impl", default="grxcp", choices=["grxcp", "reference"])
     ap.add_argument("--no-secondary", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--profile-cols", type=int, default=0,
+                    help="--profile gemm: columns of the slice (a rank's N / world); default N")
     ap.add_argument("--profile", choices=["gemm", "attention", "rmsnorm", "layernorm", "fp8", "attention_bwd",
                                           "rmsnorm_bwd", "layernorm_bwd", "conv"],
                     help="run only this kernel warmup+steps times (for ncu captures); prints no JSON")
