@@ -62,8 +62,10 @@ __device__ __forceinline__ void decode_tile(const TcGemmParams& p, int t, int& b
 // DRAM: 8192 x 1024 x 8192 went from 130 to 196 us). A unit is (tile,
 // k-blocks [kb0, kb1), split; split -1 = whole tile).
 struct WorkIter {
-  int u;
-  __device__ __forceinline__ WorkIter() : u(blockIdx.x) {}
+  int u, step;
+  __device__ __forceinline__ WorkIter() : u(blockIdx.x), step(gridDim.x) {}
+  // CTA-pair kernel: both CTAs of pair `first` walk the same units.
+  __device__ __forceinline__ WorkIter(int first, int stride) : u(first), step(stride) {}
   __device__ __forceinline__ bool next(const TcGemmParams& p, int& tile, int& kb0, int& kb1, int& split) {
     const int units = p.sk_dp_tiles + p.sk_tiles * p.sk_splits;
     if (u >= units) return false;
@@ -79,7 +81,7 @@ struct WorkIter {
       kb0 = (int)((long long)split * p.k_blocks / p.sk_splits);
       kb1 = (int)((long long)(split + 1) * p.k_blocks / p.sk_splits);
     }
-    u += gridDim.x;
+    u += step;
     return true;
   }
 };
@@ -765,7 +767,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   WaitCtx wc{p.err_word, abort_flag, p.timeout_ns};
-  const int total = p.m_tiles * p.n_tiles * p.batch;
   const int pair = blockIdx.x >> 1;
   const int npairs = gridDim.x >> 1;
 
@@ -775,13 +776,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       uint32_t armed = 0, armed_par = 0;
       bool ok = true;
-      for (int t = pair; t < total && ok; t += npairs) {
+      WorkIter it(pair, npairs);
+      int t, kb0, kb1, split;
+      while (ok && it.next(p, t, kb0, kb1, split)) {
         int bt, mt, nt;
         decode_tile(p, t, bt, mt, nt);
         const int ba = bt * p.a_batch_step, bb = bt * p.b_batch_step;
         const int row0 = mt * kPairTileM + (int)rank * 128;
         const int col0 = nt * kPairTileN + (int)rank * 128;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bounded(&empty[stage], phase ^ 1u, wc, kErrTimeoutProducer)) {
             ok = false;
             break;
@@ -835,12 +838,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
-      for (int t = pair; t < total && ok; t += npairs, ++local) {
+      WorkIter it(pair, npairs);
+      int t, kb0, kb1, split;
+      for (; ok && it.next(p, t, kb0, kb1, split); ++local) {
         const int b = local & 1;
         if (!wait_bounded(&tempty[b], ((local >> 1) & 1) ^ 1u, wc, kErrTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + b * kPairTileN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!wait_bounded(&full[stage], phase, wc, kErrTimeoutMma)) {
             ok = false;
             break;
@@ -854,7 +859,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
                                              : sw128_desc(a_addr + kk * 32, 16, 1024);
             const uint64_t bd = p.b_mn_major ? sw128_desc(b_addr + kk * UK * 128, BK * 128, 1024)
                                              : sw128_desc(b_addr + kk * 32, 16, 1024);
-            mma_ss_pair<KIND>(d_tmem, ad, bd, p.idesc, (kb | kk) != 0 ? 1u : 0u);
+            mma_ss_pair<KIND>(d_tmem, ad, bd, p.idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           mma_commit_pair(&empty[stage], 0x3);
           if (++stage == kPairStages) {
@@ -873,14 +878,50 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const int cb = ((warp - 2) >> 2) * (kPairTileN / 2);
     const int row = q * 32 + lane;
     int local = 0;
-    for (int t = pair; t < total; t += npairs, ++local) {
+    WorkIter it(pair, npairs);
+    int t, kb0, kb1, split;
+    for (; it.next(p, t, kb0, kb1, split); ++local) {
       const int b = local & 1;
       if (!wait_bounded(&tfull[b], (local >> 1) & 1, wc, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       int bt, mt, nt;
       decode_tile(p, t, bt, mt, nt);
-      epilogue_tile<KIND, OUT, PEER>(p, tmem_base + ((uint32_t)(q * 32) << 16) + b * kPairTileN, bt,
-                               mt * kPairTileM + (int)rank * 128 + row, nt * kPairTileN, cb);
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + b * kPairTileN;
+      const int grow = mt * kPairTileM + (int)rank * 128 + row;
+      bool write_c = true;
+      if (split >= 0) {
+        // A cut tile, as in the single-CTA kernel, per CTA half: each CTA of the
+        // pair owns its own 128 x 256 partial slot (slot (tile - dp) * 2 + rank)
+        // and arrival counter per epilogue warp; the last split to arrive sums
+        // all splits in split order and writes C.
+        const int r = (t - p.sk_dp_tiles) * 2 + (int)rank;
+        SkMerge mg;
+        mg.n = p.sk_splits;
+        mg.self = split;
+        mg.row = row;
+        mg.stride = (size_t)p.sk_tiles * 2 * (kTileN * kTileM);
+        mg.base = p.sk_part + (size_t)r * (kTileN * kTileM);
+        int* count = p.sk_count + (size_t)r * kEpiWarps + (warp - 2);
+        int before = 0;
+        if (split == mg.n - 1) {
+          if (lane == 0) before = ld_acquire_gpu(count);
+          before = __shfl_sync(0xffffffffu, before, 0);
+        }
+        if (before != mg.n - 1) {
+          sk_store_partial(p, t_row, p.sk_part + (size_t)r * (kTileN * kTileM) + split * mg.stride, row,
+                           nt * kPairTileN, cb, cb + kPairTileN / 2);
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) before = atomicAdd(count, 1);
+          before = __shfl_sync(0xffffffffu, before, 0);
+        }
+        write_c = before == mg.n - 1;
+        if (write_c) {
+          __threadfence();
+          sk_reduce_into_tmem<KIND>(p, t_row, mg, nt * kPairTileN, cb, cb + kPairTileN / 2);
+        }
+      }
+      if (write_c) epilogue_tile<KIND, OUT, PEER>(p, t_row, bt, grow, nt * kPairTileN, cb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -1067,9 +1108,11 @@ static bool plan_splitk(long long tiles, int k_blocks, int num_sms, SkPlan& sp) 
   return true;
 }
 
-static size_t splitk_bytes(const SkPlan& sp) {
-  const size_t parts = (size_t)sp.sk_tiles * sp.splits * kTileM * kTileN * sizeof(uint32_t);
-  const size_t counts = ((size_t)sp.sk_tiles * kEpiWarps * sizeof(int) + 255) & ~(size_t)255;
+// ctas = CTAs per tile (1, or 2 for the pair kernel: one partial slot and one
+// set of counters per CTA).
+static size_t splitk_bytes(const SkPlan& sp, int ctas = 1) {
+  const size_t parts = (size_t)sp.sk_tiles * sp.splits * ctas * kTileM * kTileN * sizeof(uint32_t);
+  const size_t counts = ((size_t)sp.sk_tiles * ctas * kEpiWarps * sizeof(int) + 255) & ~(size_t)255;
   return parts + counts;
 }
 
@@ -1079,10 +1122,13 @@ size_t tc_gemm_splitk_bytes(int kind, int m, int n, int k, int batch, int num_sm
   p.m = m;
   p.n = n;
   p.batch = batch;
-  if (use_pair(kind, p, num_sms)) return 0;
   const int bk = 128 / (kind == kKindF16 ? 2 : 1);
-  const long long tiles = (long long)((m + kTileM - 1) / kTileM) * ((n + kTileN - 1) / kTileN) * batch;
   SkPlan sp;
+  if (use_pair(kind, p, num_sms)) {
+    const long long pt = (long long)((m + kPairTileM - 1) / kPairTileM) * ((n + kPairTileN - 1) / kPairTileN) * batch;
+    return plan_splitk(pt, (k + bk - 1) / bk, num_sms / 2, sp) ? splitk_bytes(sp, 2) : 0;
+  }
+  const long long tiles = (long long)((m + kTileM - 1) / kTileM) * ((n + kTileN - 1) / kTileN) * batch;
   return plan_splitk(tiles, (k + bk - 1) / bk, num_sms, sp) ? splitk_bytes(sp) : 0;
 }
 
@@ -1203,7 +1249,28 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
     if (L.kind != kKindF16 || L.out == kOutS32) return cudaErrorNotSupported;
   }
   if (pair) {
-    const int pairs = (int)(tiles < num_sms / 2 ? tiles : num_sms / 2);
+    int pairs = (int)(tiles < num_sms / 2 ? tiles : num_sms / 2);
+    p.sk_dp_tiles = (int)tiles;
+    p.sk_tiles = 0;
+    p.sk_splits = 1;
+    SkPlan sp;
+    // Split-K tail over CTA pairs: the plan of the single-CTA kernel with a
+    // pair as the unit of parallelism; each cut unit holds two 128 x 256
+    // partial slots (one per CTA).
+    if (L.sk_ws && p.n_peers == 0 && plan_splitk(tiles, p.k_blocks, num_sms / 2, sp) &&
+        L.sk_ws_bytes >= splitk_bytes(sp, 2)) {
+      p.sk_dp_tiles = (int)sp.dp_tiles;
+      p.sk_tiles = (int)sp.sk_tiles;
+      p.sk_splits = sp.splits;
+      p.sk_part = static_cast<uint32_t*>(L.sk_ws);
+      p.sk_count = reinterpret_cast<int*>(static_cast<uint8_t*>(L.sk_ws) + (size_t)sp.sk_tiles * sp.splits * 2 *
+                                                                             kTileM * kTileN * sizeof(uint32_t));
+      const cudaError_t e =
+          cudaMemsetAsync(p.sk_count, 0, (size_t)sp.sk_tiles * 2 * kEpiWarps * sizeof(int), stream);
+      if (e != cudaSuccess) return e;
+      const long long units = sp.dp_tiles + sp.sk_tiles * sp.splits;
+      pairs = (int)(units < num_sms / 2 ? units : num_sms / 2);
+    }
     const int g2 = 2 * pairs;
     if (p.probe && p.probe_capacity < g2) return cudaErrorInvalidValue;
     if (p.n_peers > 0) {

@@ -186,3 +186,77 @@ def test_forced_schedule_runs_every_range_as_a_unit():
     grids = [dict(f.split("=", 1) for f in l.split("|")[2:])["grid"] for l in r.stderr.splitlines()
              if l.startswith("GRXPROF|1|op=launch|") and "kernel=tc_gemm_kernel" in l]
     assert grids == ["45.1.1"], grids  # 15 tiles x 3 ranges; whole tiles would launch 15 CTAs
+
+
+# ------------------------------------------------------------------ the CTA-pair kernel's split-K tail
+
+@pytest.mark.parametrize("splits", [2, 5])
+@pytest.mark.parametrize("ta,tb", [(1, 0), (0, 1)])
+def test_pair_splitk_int8_exact_with_beta(blas, splits, ta, tb, monkeypatch):
+    """The pair kernel with every 256 x 256 tile cut into `splits` k-ranges:
+    each CTA of a pair publishes its own 128-row half; integer partials summed
+    exactly in split order; ld padding of C untouched."""
+    monkeypatch.setenv("GRX_GEMM_FORCE_PAIR", "1")
+    monkeypatch.setenv("GRX_GEMM_FORCE_SK", str(splits))
+    m, n, k, pad = 600, 700, 4096, 8
+    a_rows, a_cols = (k, m) if ta else (m, k)
+    b_rows, b_cols = (n, k) if tb else (k, n)
+    lda, ldb, ldc = a_rows + pad, b_rows + pad, m + pad
+    A, B, C = int8_patterns(lda * a_cols, ldb * b_cols, ldc * n)
+    want = oracle.igemm(ta, tb, m, n, k, 3, A, lda, B, ldb, -2, C, ldc)
+    dC = torch.from_numpy(C.copy()).cuda()
+    st = blas.gemm_ex(ta, tb, m, n, k, 3.0, dev_bits(A), N.GRX_R_8I, lda, dev_bits(B), N.GRX_R_8I, ldb, -2.0, dC,
+                      N.GRX_R_32I, ldc)
+    assert st == N.SUCCESS
+    torch.cuda.synchronize()
+    assert blas.execution_status() == N.SUCCESS
+    assert np.array_equal(dC.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("splits", [3, 8])
+def test_pair_splitk_bf16_bias_gelu_ragged(blas, splits, monkeypatch):
+    monkeypatch.setenv("GRX_GEMM_FORCE_PAIR", "1")
+    monkeypatch.setenv("GRX_GEMM_FORCE_SK", str(splits))
+    m, n, k = 333, 517, 1000
+    A, B, bias = bf16_problem(m, n, k, 43)
+    lin = oracle.gemm_f64(1, 0, m, n, k, 1.0, A, k, B, k).reshape(n, m).T + bias[None, :]
+    want = oracle.gelu(lin.astype(np.float32), 1)
+    dC = torch.full((m * n,), float("nan"), dtype=torch.bfloat16, device="cuda")
+    dbias = dev_f32(bias)
+    assert blas.set_epilogue(bias=dbias, bias_type=N.GRX_R_32F, activation=N.ACT_GELU_TANH) == N.SUCCESS
+    st = blas.gemm_ex(1, 0, m, n, k, 1.0, dev_bits(oracle.encode("bf16", A)), N.GRX_R_16BF, k,
+                      dev_bits(oracle.encode("bf16", B)), N.GRX_R_16BF, k, 0.0, dC, N.GRX_R_16BF, m)
+    assert st == N.SUCCESS
+    torch.cuda.synchronize()
+    assert blas.execution_status() == N.SUCCESS
+    ok, nbad = close(dC.float().cpu().numpy().reshape(n, m).T, want)
+    assert ok, f"{nbad} elements out of tolerance"
+
+
+def test_pair_splitk_automatic_plan_on_the_four_gpu_slice(blas):
+    """8192 x 2048 x 8192 bf16 + bias (one rank's slice at 4 GPUs): 256 pair
+    tiles on 74 SM pairs, whose last partial round the planner cuts in two.
+    Sampled full columns (first, last, tile seams, random) against the fp64
+    oracle; a repeat call is bit-identical (deterministic reduction)."""
+    m, n, k = 8192, 2048, 8192
+    g = torch.Generator(device="cuda").manual_seed(12)
+    dA = (torch.randn(k, m, device="cuda", generator=g) / k ** 0.5).to(torch.bfloat16)
+    dB = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).to(torch.bfloat16)
+    dbias = torch.randn(n, device="cuda", generator=g) * 0.02
+    dC = torch.empty(n, m, dtype=torch.bfloat16, device="cuda")
+    assert blas.set_epilogue(bias=dbias, bias_type=N.GRX_R_32F) == N.SUCCESS
+    call = lambda c: blas.gemm_ex(1, 0, m, n, k, 1.0, dA, N.GRX_R_16BF, k, dB, N.GRX_R_16BF, k, 0.0, c,  # noqa: E731
+                                  N.GRX_R_16BF, m)
+    assert call(dC) == N.SUCCESS
+    dC2 = torch.empty_like(dC)
+    assert call(dC2) == N.SUCCESS
+    torch.cuda.synchronize()
+    assert blas.execution_status() == N.SUCCESS
+    assert torch.equal(dC, dC2)
+    cols = np.unique(np.concatenate([[0, 1, 255, 256, 1791, 1792, n - 1], np.random.default_rng(4).integers(0, n, 9)]))
+    A = dA.float().cpu().numpy().ravel()
+    Bsub = dB[torch.as_tensor(cols, device="cuda")].float().cpu().numpy().ravel()
+    want = oracle.gemm_f64(1, 0, m, len(cols), k, 1.0, A, k, Bsub, k, bias=dbias.cpu().numpy()[cols])
+    got = dC[torch.as_tensor(cols, device="cuda")].float().cpu().numpy().ravel()
+    ok, nbad = close(got, want)
+    assert ok, f"{nbad} of {got.size} out of tolerance"
