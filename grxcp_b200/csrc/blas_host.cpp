@@ -480,7 +480,7 @@ grxblasStatus_t grxblasSetCycleProbe(grxblasHandle_t handle, grxCycleSlot* slots
 // Slots for an m x n call of either kernel family: the sgemm grid (at batch 1,
 // the smallest tile, so batch x this covers every batched call), or the
 // tensor-core GEMM's persistent grid, which never exceeds the SM count nor two
-// CTAs per 128 x 256 tile.
+// CTAs per 128 x 32 block of C.
 int grxblasCycleSlotsNeeded(grxblasHandle_t handle, int m, int n) {
   (void)handle;
   if (m <= 0 || n <= 0) return 0;
@@ -490,7 +490,9 @@ int grxblasCycleSlotsNeeded(grxblasHandle_t handle, int m, int n) {
     sms = 148;  // no device: B200's count
   }
   const int sg = grx::sgemm_ctas(m, n, 1, sms);
-  const long long tiles = 2LL * ((m + grx::kTileM - 1) / grx::kTileM) * ((n + grx::kTileN - 1) / grx::kTileN);
+  // tensor-core grid: at most one CTA per SM; with few tiles the single-CTA
+  // kernel narrows them down to 32 columns (more CTAs)
+  const long long tiles = 2LL * ((m + grx::kTileM - 1) / grx::kTileM) * ((n + 31) / 32);
   const int tc = (int)(tiles < sms ? tiles : sms);
   return sg > tc ? sg : tc;
 }

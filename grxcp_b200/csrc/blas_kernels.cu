@@ -3,6 +3,7 @@
 // path, and level-1/2 BLAS.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <stdlib.h>
 
 #include "activation.cuh"
 #include "kernels.h"
@@ -19,8 +20,9 @@ namespace grx {
 // element strides, beta == 0 never reads C. Instead of one thread per output
 // with two global loads per multiply-add, a BM x BN output tile per CTA is
 // staged through shared memory in k-slabs of BK and each thread accumulates a
-// TM x TN sub-tile in registers (fp32 FMA, one accumulator per output, k in
-// ascending order, so every tile shape gives the same bits).
+// TM x TN sub-tile in registers (fp32 FMA, k in ascending order; one
+// accumulator per output for KG = 1, KG accumulators summed in a fixed order
+// otherwise, so every call of a shape gives the same bits).
 //
 // The slabs stream through an ST-deep cp.async ring (4-byte copies with
 // zero fill past the matrix edge), so the global-load latency of slab t + ST - 1
@@ -28,9 +30,17 @@ namespace grx {
 // trip. The tile shape follows the grid: 128 x 128 once that fills the SMs,
 // else 64 x 64, else 32 x 32 (a 512^3 problem is 16 CTAs of 128 x 128 but 256
 // of 32 x 32).
-template <int BM, int BN, int BK, int TM, int TN, int ST>
+//
+// KG > 1 splits each slab's k-steps over KG thread groups of one CTA (group
+// g takes steps [g BK / KG, (g + 1) BK / KG) of every slab, in order), and
+// group 0 adds the other groups' sub-tiles in group order through shared
+// memory before the epilogue: deterministic, and KG times the warps per CTA
+// for the small problems whose grid cannot fill the SMs (the 32 x 32 tiles:
+// 64 threads, one warp per SM sub-partition at 512^3, was latency-bound).
+template <int BM, int BN, int BK, int TM, int TN, int ST, int KG = 1>
 struct SgemmCfg {
-  static constexpr int kThreads = (BM / TM) * (BN / TN);
+  static constexpr int kT0 = (BM / TM) * (BN / TN);  // threads of one k-group
+  static constexpr int kThreads = kT0 * KG;
   static constexpr int kGx = BM / TM;  // threads along m
   static constexpr int kPadM = BM + 4, kPadN = BN + 4;  // +4 floats: the k-fastest fill is conflict-free
 };
@@ -45,14 +55,17 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <int BM, int BN, int BK, int TM, int TN, int ST>
-__global__ void __launch_bounds__(SgemmCfg<BM, BN, BK, TM, TN, ST>::kThreads) sgemm_kernel(SgemmArgs p) {
-  using Cfg = SgemmCfg<BM, BN, BK, TM, TN, ST>;
+template <int BM, int BN, int BK, int TM, int TN, int ST, int KG>
+__global__ void __launch_bounds__(SgemmCfg<BM, BN, BK, TM, TN, ST, KG>::kThreads) sgemm_kernel(SgemmArgs p) {
+  using Cfg = SgemmCfg<BM, BN, BK, TM, TN, ST, KG>;
   constexpr int NT = Cfg::kThreads;
+  constexpr int KS = BK / KG;  // k-steps of one group per slab
   static_assert((BM * BK) % NT == 0 && (BN * BK) % NT == 0, "slab must split evenly over the threads");
   static_assert(TM % 4 == 0 && TN % 4 == 0, "sub-tiles are read as float4 groups");
+  static_assert(BK % KG == 0, "k-groups split each slab evenly");
   __shared__ __align__(16) float As[ST][BK][Cfg::kPadM];
   __shared__ __align__(16) float Bs[ST][BK][Cfg::kPadN];
+  __shared__ float Red[KG > 1 ? (KG - 1) * TM * TN * Cfg::kT0 : 1];
   long long t_start = 0;
   if (p.probe) t_start = clock64();
 
@@ -62,7 +75,8 @@ __global__ void __launch_bounds__(SgemmCfg<BM, BN, BK, TM, TN, ST>::kThreads) sg
   float* C = p.c + (long long)bz * p.stride_c;
   const int m0 = blockIdx.x * BM, n0 = blockIdx.y * BN;
   const int tid = threadIdx.x;
-  const int tx = tid % Cfg::kGx, ty = tid / Cfg::kGx;
+  const int t0 = tid % Cfg::kT0, kgrp = tid / Cfg::kT0;
+  const int tx = t0 % Cfg::kGx, ty = t0 / Cfg::kGx;
 
   // One slab: element (r, l) of op(A) to As[slot][l][r], (l, c) of op(B) to
   // Bs[slot][l][c]. Consecutive threads take the operand's contiguous direction.
@@ -111,7 +125,8 @@ __global__ void __launch_bounds__(SgemmCfg<BM, BN, BK, TM, TN, ST>::kThreads) sg
     cp_async_commit();
     const int cur = t % ST;
 #pragma unroll
-    for (int l = 0; l < BK; ++l) {
+    for (int ll = 0; ll < KS; ++ll) {
+      const int l = kgrp * KS + ll;
       float a[TM], b[TN];
 #pragma unroll
       for (int g = 0; g < TM / 4; ++g) {
@@ -130,6 +145,22 @@ __global__ void __launch_bounds__(SgemmCfg<BM, BN, BK, TM, TN, ST>::kThreads) sg
     }
   }
   cp_async_wait<0>();
+  if constexpr (KG > 1) {
+    if (kgrp > 0) {
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) Red[(((kgrp - 1) * TM + i) * TN + j) * Cfg::kT0 + t0] = acc[i][j];
+    }
+    __syncthreads();
+    if (kgrp > 0) return;
+#pragma unroll 1
+    for (int g = 0; g < KG - 1; ++g)
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] += Red[((g * TM + i) * TN + j) * Cfg::kT0 + t0];
+  }
 
 #pragma unroll
   for (int j = 0; j < TN; ++j) {
@@ -174,13 +205,13 @@ int sgemm_ctas(int m, int n, int batch, int num_sms) {
   return ((m + t - 1) / t) * ((n + t - 1) / t) * batch;
 }
 
-template <int BM, int BK, int TM, int ST>
+template <int BM, int BK, int TM, int ST, int KG = 1>
 static cudaError_t sgemm_go(const SgemmArgs& a, cudaStream_t s) {
-  constexpr int NT = SgemmCfg<BM, BM, BK, TM, TM, ST>::kThreads;
+  constexpr int NT = SgemmCfg<BM, BM, BK, TM, TM, ST, KG>::kThreads;
   dim3 grid((a.m + BM - 1) / BM, (a.n + BM - 1) / BM, a.batch);
   if (grid.y > 65535u || grid.z > 65535u) return cudaErrorInvalidValue;
   ProfLaunch prof("sgemm_kernel", grid, dim3(NT), 0, s);
-  sgemm_kernel<BM, BM, BK, TM, TM, ST><<<grid, NT, 0, s>>>(a);
+  sgemm_kernel<BM, BM, BK, TM, TM, ST, KG><<<grid, NT, 0, s>>>(a);
   return cudaGetLastError();
 }
 
@@ -188,7 +219,9 @@ cudaError_t launch_sgemm(const SgemmArgs& a, int num_sms, cudaStream_t s) {
   switch (sgemm_tile(a.m, a.n, a.batch, num_sms)) {
     case 128: return sgemm_go<128, 8, 8, 4>(a, s);
     case 64: return sgemm_go<64, 16, 4, 4>(a, s);
-    default: return sgemm_go<32, 16, 4, 4>(a, s);
+    // k-groups pay once k is long enough to amortise their final reduction
+    default: return (a.k >= 256 && !getenv("GRX_SGEMM_KG1")) ? sgemm_go<32, 16, 4, 4, 4>(a, s)
+                                                              : sgemm_go<32, 16, 4, 4>(a, s);
   }
 }
 

@@ -354,10 +354,11 @@ __device__ __forceinline__ void epi_chunk(const TcGemmParams& p, const EpiRow& e
 constexpr int kEpiChunks = kTileN / 2 / 32;  // chunks of one epilogue warp's column half
 
 template <int KIND, int OUT, bool PEER = false>
-__device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_row, int bt, int i, int col0, int cb) {
+__device__ __forceinline__ void epilogue_tile(const TcGemmParams& p, uint32_t t_row, int bt, int i, int col0, int cb,
+                                              int width = kTileN) {
   constexpr int kOutBytes = (OUT == kOutBF16 || OUT == kOutF16) ? 2 : 4;
   const int lane = threadIdx.x & 31;
-  int cols = p.n - col0 - cb;
+  int cols = min(p.n - col0, width) - cb;
   if (cols > kEpiChunks * 32) cols = kEpiChunks * 32;
   const int nch = (cols + 31) / 32;
   if (nch <= 0) return;  // warp-uniform
@@ -467,7 +468,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int UK = 32 / ES;                     // k per tcgen05.mma
   constexpr int KSUB = BK / UK;                   // MMAs per stage
   constexpr int ATOM = 128 / ES;                  // elements in one MN-major swizzle row
-  constexpr uint32_t kStageTx = kStageBytesA + kStageBytesB;
+  // Output columns per tile: kTileN, or fewer for problems with fewer tiles
+  // than SMs (launch_tc_gemm); the B box then holds TN rows (K-major) or
+  // TN / ATOM atoms (MN-major) and the MMA runs with N = TN.
+  const int TN = CONV ? kTileN : p.tile_n;
 
   if (p.abi_version != kTcGemmAbi) {
     if (threadIdx.x == 0 && p.err_word) atomicCAS(p.err_word, 0, kErrBadAbi);
@@ -536,7 +540,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           }
           uint64_t* fb = &full[stage];
-          mbar_arrive_expect_tx(fb, CONV ? (uint32_t)kStageBytesA + p.cv_b_bytes : kStageTx);
+          mbar_arrive_expect_tx(fb, CONV ? (uint32_t)kStageBytesA + p.cv_b_bytes : (uint32_t)(kStageBytesA + TN * 128));
           issued_mask |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
           uint8_t* a_dst = sA + stage * kStageBytesA;
@@ -561,11 +565,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tma_load_4d(b_dst, &tmB, fb, c0, q0 * p.cv_sw - p.cv_pw + fs * p.cv_dw,
                         p0 * p.cv_sh - p.cv_ph + fr * p.cv_dh, img);
           } else if (!p.b_mn_major) {
-            tma_load_3d(b_dst, &tmB, fb, k0, nt * kTileN, bb);
+            tma_load_3d(b_dst, &tmB, fb, k0, nt * TN, bb);
           } else {
-#pragma unroll
-            for (int j = 0; j < kTileN / ATOM; ++j)
-              tma_load_3d(b_dst + j * (BK * 128), &tmB, fb, nt * kTileN + j * ATOM, k0, bb);
+            for (int j = 0; j < TN / ATOM; ++j)
+              tma_load_3d(b_dst + j * (BK * 128), &tmB, fb, nt * TN + j * ATOM, k0, bb);
           }
           if (++stage == kStages) {
             stage = 0;
@@ -641,7 +644,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if constexpr (CONV) {
         epilogue_conv<KIND, OUT>(p, t_row, mt * kTileM + row, nt, cb);
       } else if (split < 0) {
-        epilogue_tile<KIND, OUT, PEER>(p, t_row, bt, mt * kTileM + row, nt * kTileN, cb);
+        epilogue_tile<KIND, OUT, PEER>(p, t_row, bt, mt * kTileM + row, nt * TN, cb, TN);
       } else {
         // A cut tile: publish this unit's partial, count it in, and let the
         // last split of the tile to arrive reduce and write C. Nobody waits on
@@ -1201,6 +1204,7 @@ cudaError_t launch_tc_conv(const TcConvLaunch& L, int num_sms, cudaStream_t stre
   p.b_mn_major = 0;
   p.a_batch_step = p.b_batch_step = 0;
   p.idesc = make_idesc(1u, 1u, 1u, 0u, 0u, kTileM, kTileN);
+  p.tile_n = kTileN;
   p.sk_dp_tiles = (int)tiles;
   p.sk_tiles = 0;
   p.sk_splits = 1;
@@ -1219,10 +1223,32 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
   p.abi_version = kTcGemmAbi;
   const int bk = 128 / es;
   const bool pair = use_pair(L.kind, p, num_sms);
-  const int tile_m = pair ? kPairTileM : kTileM, tile_n = pair ? kPairTileN : kTileN;
+  const int tile_m = pair ? kPairTileM : kTileM;
+  int tile_n = pair ? kPairTileN : kTileN;
   p.m_tiles = (p.m + tile_m - 1) / tile_m;
   p.n_tiles = (p.n + tile_n - 1) / tile_n;
   p.k_blocks = (p.k + bk - 1) / bk;
+  // Single-CTA kernel: a split-K tail for few tiles with long K; otherwise,
+  // while the tiles fill at most half the SMs, halve the tile's columns (down
+  // to 32; an MN-major B keeps whole 128-byte atoms) so more SMs share the
+  // MMAs and, above all, the epilogue's stores (int8 512^3:
+  // 8 CTAs of 128 x 256 become 64 of 128 x 32).
+  SkPlan sp;
+  bool splitk = false;
+  if (!pair) {
+    const long long tiles256 = (long long)p.m_tiles * p.n_tiles * p.batch;
+    splitk = L.sk_ws && plan_splitk(tiles256, p.k_blocks, num_sms, sp) && L.sk_ws_bytes >= splitk_bytes(sp);
+    const int min_tn = L.b_mn_major ? 128 / es : 32;
+    if (!splitk && !getenv("GRX_GEMM_WIDE_TILES")) {
+      while (tile_n / 2 >= min_tn) {
+        const long long t2 = (long long)p.m_tiles * ((p.n + tile_n / 2 - 1) / (tile_n / 2)) * p.batch;
+        if (t2 > num_sms) break;
+        tile_n /= 2;
+      }
+      p.n_tiles = (p.n + tile_n - 1) / tile_n;
+    }
+  }
+  p.tile_n = tile_n;
   if (p.group_m <= 0) p.group_m = 16;
   p.a_mn_major = L.a_mn_major;
   p.b_mn_major = L.b_mn_major;
@@ -1230,7 +1256,7 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
   // epilogue converts to the requested output type.
   const uint32_t cfmt = (L.kind == kKindI8) ? 2u : 1u;
   p.idesc = make_idesc(cfmt, (uint32_t)L.a_fmt, (uint32_t)L.a_fmt, (uint32_t)L.a_mn_major, (uint32_t)L.b_mn_major,
-                       pair ? kPairTileM : kTileM, pair ? kPairTileN : kTileN);
+                       pair ? kPairTileM : kTileM, pair ? kPairTileN : tile_n);
   const int a_bdim = (p.batch > 1 && L.stride_a != 0) ? p.batch : 1;
   const int b_bdim = (p.batch > 1 && L.stride_b != 0) ? p.batch : 1;
   p.a_batch_step = a_bdim > 1 ? 1 : 0;
@@ -1240,7 +1266,7 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
   // CTA of a pair) of B.
   if (!make_operand_map(&ma, L.a, es, L.a_mn_major, p.m, p.k, L.lda, L.stride_a, a_bdim, 128))
     return cudaErrorInvalidValue;
-  if (!make_operand_map(&mb, L.b, es, L.b_mn_major, p.n, p.k, L.ldb, L.stride_b, b_bdim, pair ? 128 : kTileN))
+  if (!make_operand_map(&mb, L.b, es, L.b_mn_major, p.n, p.k, L.ldb, L.stride_b, b_bdim, pair ? 128 : tile_n))
     return cudaErrorInvalidValue;
   const long long tiles = (long long)p.m_tiles * p.n_tiles * p.batch;
   if (tiles > 0x7fffffffLL) return cudaErrorInvalidValue;
@@ -1297,8 +1323,7 @@ cudaError_t launch_tc_gemm(const TcGemmLaunch& L, int num_sms, cudaStream_t stre
   p.sk_dp_tiles = (int)tiles;
   p.sk_tiles = 0;
   p.sk_splits = 1;
-  SkPlan sp;
-  if (L.sk_ws && plan_splitk(tiles, p.k_blocks, num_sms, sp) && L.sk_ws_bytes >= splitk_bytes(sp)) {
+  if (splitk) {
     p.sk_dp_tiles = (int)sp.dp_tiles;
     p.sk_tiles = (int)sp.sk_tiles;
     p.sk_splits = sp.splits;

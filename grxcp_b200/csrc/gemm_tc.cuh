@@ -13,7 +13,7 @@ namespace grx {
 // The kernel refuses to run on a version mismatch (the reference's kernel ABI
 // blocks do the same, src/libs/grxblas/hgemm_abi.h:20 and
 // src/libs/grxblas/kernels/sgemm.cpp:23-27).
-constexpr uint32_t kTcGemmAbi = 7;
+constexpr uint32_t kTcGemmAbi = 8;
 constexpr int kMaxPeers = 7;  // one process per GPU, eight GPUs per node
 
 enum TcKind : int { kKindF16 = 0, kKindI8 = 1, kKindF8 = 2 };
@@ -26,6 +26,7 @@ struct TcGemmParams {
   int a_batch_step, b_batch_step;  // 1: batch coordinate walks the tensor map, 0: broadcast
   int m_tiles, n_tiles, k_blocks;
   int group_m;                     // rasterisation band height in m-tiles
+  int tile_n;                      // single-CTA kernel: output columns per tile (32..256, see launch_tc_gemm)
   uint32_t idesc;                  // tcgen05 instruction descriptor
   float alpha, beta;
   int ialpha, ibeta;               // int32 epilogue (exact int8 path)
