@@ -63,9 +63,13 @@ __global__ void __launch_bounds__(SgemmCfg<BM, BN, BK, TM, TN, ST, KG>::kThreads
   static_assert((BM * BK) % NT == 0 && (BN * BK) % NT == 0, "slab must split evenly over the threads");
   static_assert(TM % 4 == 0 && TN % 4 == 0, "sub-tiles are read as float4 groups");
   static_assert(BK % KG == 0, "k-groups split each slab evenly");
-  __shared__ __align__(16) float As[ST][BK][Cfg::kPadM];
-  __shared__ __align__(16) float Bs[ST][BK][Cfg::kPadN];
-  __shared__ float Red[KG > 1 ? (KG - 1) * TM * TN * Cfg::kT0 : 1];
+  // The k-groups' partial sub-tiles reuse the slab ring once it is drained.
+  constexpr int kRing = ST * BK * (Cfg::kPadM + Cfg::kPadN);
+  constexpr int kRed = (KG - 1) * TM * TN * Cfg::kT0;
+  __shared__ __align__(16) float smem[kRing > kRed ? kRing : kRed];
+  auto As = reinterpret_cast<float (*)[BK][Cfg::kPadM]>(smem);
+  auto Bs = reinterpret_cast<float (*)[BK][Cfg::kPadN]>(smem + ST * BK * Cfg::kPadM);
+  float* Red = smem;
   long long t_start = 0;
   if (p.probe) t_start = clock64();
 
@@ -146,6 +150,7 @@ __global__ void __launch_bounds__(SgemmCfg<BM, BN, BK, TM, TN, ST, KG>::kThreads
   }
   cp_async_wait<0>();
   if constexpr (KG > 1) {
+    __syncthreads();  // every group is done reading the ring
     if (kgrp > 0) {
 #pragma unroll
       for (int i = 0; i < TM; ++i)
@@ -219,9 +224,15 @@ cudaError_t launch_sgemm(const SgemmArgs& a, int num_sms, cudaStream_t s) {
   switch (sgemm_tile(a.m, a.n, a.batch, num_sms)) {
     case 128: return sgemm_go<128, 8, 8, 4>(a, s);
     case 64: return sgemm_go<64, 16, 4, 4>(a, s);
-    // k-groups pay once k is long enough to amortise their final reduction
-    default: return (a.k >= 256 && !getenv("GRX_SGEMM_KG1")) ? sgemm_go<32, 16, 4, 4, 4>(a, s)
-                                                              : sgemm_go<32, 16, 4, 4>(a, s);
+    // 32 x 32 tiles: 4 k-groups once k is long enough to amortise their final
+    // reduction, over 32-deep slabs in a 3-stage ring. Measured at 512^3 (device
+    // time, CUDA-graph replay): one group 37 us; 4 groups with 16-deep slabs
+    // 22.8 (4 stages) / 23.1 (6 stages); 32-deep slabs 20.9 (3 stages) / 21.4 (4);
+    // 8 groups 21.8 (32-deep) / 23.9 (64-deep, 2 stages); 2 groups 28.5.
+    // GRX_SGEMM_KG1=1 keeps one group (A/B measurements).
+    default:
+      return (a.k >= 256 && !getenv("GRX_SGEMM_KG1")) ? sgemm_go<32, 32, 4, 3, 4>(a, s)
+                                                        : sgemm_go<32, 16, 4, 4>(a, s);
   }
 }
 
