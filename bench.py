@@ -653,6 +653,36 @@ def run_profile(args):
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(1)
     n_iter = args.warmup + args.steps
+    if args.profile == "config1":
+        # BASELINE config 1 (512^3): int8 and bf16 GemmEx with the narrow tiles, then with
+        # 128 x 256 tiles (GRX_GEMM_WIDE_TILES), then SGEMM with 4 k-groups and with one.
+        h = B.Handle()
+        ia = torch.randint(-128, 128, (512 * 512,), dtype=torch.int8, device=dev, generator=g)
+        ic = torch.empty(512 * 512, dtype=torch.int32, device=dev)
+        ba = torch.randn(512 * 512, device=dev, generator=g).to(torch.bfloat16)
+        bc = torch.empty(512 * 512, device=dev, dtype=torch.bfloat16)
+        fa = torch.rand(512 * 512, device=dev, generator=g) * 2 - 1
+        fc = torch.empty(512 * 512, device=dev)
+        for env in (None, "GRX_GEMM_WIDE_TILES"):
+            if env:
+                os.environ[env] = "1"
+            for _ in range(n_iter):
+                B.check(h.gemm_ex(0, 0, 512, 512, 512, 1.0, ia, Nn.GRX_R_8I, 512, ia, Nn.GRX_R_8I, 512, 0.0, ic,
+                                  Nn.GRX_R_32I, 512))
+            for _ in range(n_iter):
+                B.check(h.gemm_ex(1, 0, 512, 512, 512, 1.0, ba, Nn.GRX_R_16BF, 512, ba, Nn.GRX_R_16BF, 512, 0.0, bc,
+                                  Nn.GRX_R_16BF, 512))
+            os.environ.pop("GRX_GEMM_WIDE_TILES", None)
+        for env in (None, "GRX_SGEMM_KG1"):
+            if env:
+                os.environ[env] = "1"
+            for _ in range(n_iter):
+                B.check(h.sgemm(0, 0, 512, 512, 512, 1.0, fa, 512, fa, 512, 0.0, fc, 512))
+            os.environ.pop("GRX_SGEMM_KG1", None)
+        torch.cuda.synchronize()
+        B.check(h.execution_status())
+        h.close()
+        return
     if args.profile in ("gemm", "fp8"):
         h = B.Handle()
         if args.profile == "gemm":
@@ -738,7 +768,7 @@ def main():
     ap.add_argument("--profile-cols", type=int, default=0,
                     help="--profile gemm: columns of the slice (a rank's N / world); default N")
     ap.add_argument("--profile", choices=["gemm", "attention", "rmsnorm", "layernorm", "fp8", "attention_bwd",
-                                          "rmsnorm_bwd", "layernorm_bwd", "conv"],
+                                          "rmsnorm_bwd", "layernorm_bwd", "conv", "config1"],
                     help="run only this kernel warmup+steps times (for ncu captures); prints no JSON")
     args = ap.parse_args()
     if args.impl == "reference":
