@@ -152,3 +152,38 @@ def test_norm_backward_empty_and_errors(dh):
                                      1e-5, p, N.GRX_R_16BF, 64, None) == N.INVALID_VALUE
     assert lib.grxdnnRMSNormBackward(None, 8, 64, p, N.GRX_R_16BF, 64, p, N.GRX_R_16BF, 64, g.data_ptr(), None,
                                      1e-5, p, N.GRX_R_16BF, 64, None) == N.NOT_INITIALIZED
+
+
+@pytest.mark.parametrize("ln", [False, True])
+def test_norm_backward_l2_prefetch_changes_no_bits(dh, ln, monkeypatch):
+    """The dense kernels ask L2 for each CTA's next row (bulk prefetch); that
+    moves no data the arithmetic sees, so dx, dgamma and dbeta equal the
+    results with the prefetch off (GRX_NORM_BWD_NO_PREFETCH=1) bit for bit."""
+    rows, hidden = 3000, 8192
+    xs, ds, gamma, beta = _inputs(rows, hidden, "bf16", 21)
+    x, dy, gm, bt = xs.cuda(), ds.cuda(), gamma.cuda(), beta.cuda()
+    mean = torch.empty(rows, device="cuda")
+    rstd = torch.empty(rows, device="cuda")
+    y = torch.empty_like(x)
+    assert (dh.layernorm(x, gm, bt, 1e-5, y, mean, rstd) if ln else dh.rmsnorm(x, gm, 1e-5, y, rstd)) == N.SUCCESS
+
+    def run():
+        dx = torch.full_like(x, float("nan"))
+        dg = torch.full((hidden,), float("nan"), device="cuda")
+        db = torch.full((hidden,), float("nan"), device="cuda")
+        if ln:
+            st = dh.layernorm_backward(dy, x, gm, 1e-5, dx, mean, rstd, dg, db)
+        else:
+            st = dh.rmsnorm_backward(dy, x, gm, 1e-5, dx, rstd, dg)
+        assert st == N.SUCCESS
+        torch.cuda.synchronize()
+        assert dh.execution_status() == N.SUCCESS
+        return dx, dg, db
+
+    a = run()
+    monkeypatch.setenv("GRX_NORM_BWD_NO_PREFETCH", "1")
+    b = run()
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+    if ln:
+        assert torch.equal(a[2], b[2])
+    _check(ln, "bf16", xs, ds, gamma, a[0].cpu(), a[1], a[2] if ln else None, hidden)
