@@ -546,6 +546,13 @@ def run_secondary(args, peaks, dev, stream):
     nb = nbytes + 8192 * 4
     out["layernorm"] = {"value": nb / ms / 1e6, "unit": "GB/s", "ms": ms, "frac": nb / ms / 1e6 / hbm,
                         "config": "bf16 [65536, 8192], fp32 gamma/beta, eps 1e-5"}
+    # softmax over rows and GELU on the same bf16 tensor: read once, written once
+    ms = _time(lambda: dh.softmax(x, y), 20, stream)
+    out["softmax"] = {"value": (nbytes - 8192 * 4) / ms / 1e6, "unit": "GB/s", "ms": ms,
+                      "frac": (nbytes - 8192 * 4) / ms / 1e6 / hbm, "config": "bf16 [65536, 8192], fp32 math"}
+    ms = _time(lambda: dh.gelu(x, y, 0), 20, stream)
+    out["gelu"] = {"value": (nbytes - 8192 * 4) / ms / 1e6, "unit": "GB/s", "ms": ms,
+                   "frac": (nbytes - 8192 * 4) / ms / 1e6 / hbm, "config": "bf16, 2^29 elements, erf form"}
     # norm backward on the same shape: x and dy read, dx written (saved statistics)
     dy = torch.randn(65536, 8192, device=dev, generator=g).to(torch.bfloat16)
     mean = torch.empty(65536, device=dev)

@@ -81,6 +81,8 @@ __global__ void __launch_bounds__(kThreads) softmax_vec_kernel(int cols, const T
     }
   }
   mx = block_reduce<true>(mx, red);
+  // Each exponential is computed once and kept in registers for the output.
+  float pe[NV][EPV];
   float sum = 0.f;
 #pragma unroll
   for (int v = 0; v < NV; ++v) {
@@ -88,7 +90,10 @@ __global__ void __launch_bounds__(kThreads) softmax_vec_kernel(int cols, const T
     if (vi < nvec) {
       const T* e = reinterpret_cast<const T*>(&buf[v]);
 #pragma unroll
-      for (int q = 0; q < EPV; ++q) sum += expf(E<T>::f(e[q]) - mx);
+      for (int q = 0; q < EPV; ++q) {
+        pe[v][q] = expf(E<T>::f(e[q]) - mx);
+        sum += pe[v][q];
+      }
     }
   }
   const float inv = 1.f / block_reduce<false>(sum, red + 32);
@@ -96,11 +101,10 @@ __global__ void __launch_bounds__(kThreads) softmax_vec_kernel(int cols, const T
   for (int v = 0; v < NV; ++v) {
     const int vi = threadIdx.x + v * kThreads;
     if (vi < nvec) {
-      const T* e = reinterpret_cast<const T*>(&buf[v]);
       uint4 o;
       T* oe = reinterpret_cast<T*>(&o);
 #pragma unroll
-      for (int q = 0; q < EPV; ++q) oe[q] = E<T>::t(expf(E<T>::f(e[q]) - mx) * inv);
+      for (int q = 0; q < EPV; ++q) oe[q] = E<T>::t(pe[v][q] * inv);
       __stcs(yr + vi, o);
     }
   }
@@ -145,23 +149,82 @@ cudaError_t softmax_dispatch(int rows, int cols, const void* x, long long ldx, v
   return cudaGetLastError();
 }
 
+// GELU (erf form) for 16-bit outputs: x * Phi(x) with erf from Abramowitz &
+// Stegun, Handbook of Mathematical Functions (1964), formula 7.1.26 (after
+// Hastings): for a = |z|, t = 1 / (1 + p a),
+//   1 - erf(a) = (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) exp(-a^2),
+// absolute error <= 1.5e-7. With q = that right-hand side, 1 + erf(z) is q for
+// z < 0 and 2 - q otherwise, so the far negative tail keeps its small values
+// instead of cancelling. The reciprocal and 2^x are the SFU's approximate
+// instructions; the result's absolute error stays below 1e-6 * |x|, far under
+// a 16-bit output's rounding. In the far negative tail, where x Phi(x) is tiny,
+// the relative error grows: 0.16 % at x = -5, a few % from x = -8 on (values
+// below 1e-14 there). fp32 outputs keep erff.
+__device__ __forceinline__ float gelu_erf_as(float x) {
+  const float z = x * 0.7071067811865476f;
+  const float a = fabsf(z);
+  float t;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(t) : "f"(fmaf(0.3275911f, a, 1.f)));
+  float poly = fmaf(1.061405429f, t, -1.453152027f);
+  poly = fmaf(poly, t, 1.421413741f);
+  poly = fmaf(poly, t, -0.284496736f);
+  poly = fmaf(poly, t, 0.254829592f);
+  poly *= t;
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-a * a * 1.4426950408889634f));
+  const float q = poly * e;
+  const float one_plus_erf = z < 0.f ? q : 2.f - q;
+  return 0.5f * x * one_plus_erf;
+}
+
+// The forward GELU of one element: the erf form through gelu_erf_as for
+// 16-bit types, the shared epilogue activation otherwise.
+template <typename T>
+__device__ __forceinline__ float gelu_value(float v, int act) {
+  if (sizeof(T) == 2 && act == kActGeluErf) return gelu_erf_as(v);
+  return apply_act(v, act);
+}
+
 template <typename T>
 __global__ void gelu_kernel(long long n, const T* x, T* y, int act, int vec) {
   constexpr int EPV = 16 / sizeof(T);
+  constexpr int U = 4;  // vectors in flight per thread
   const long long stride = (long long)gridDim.x * blockDim.x;
   const long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   if (vec) {
     const long long nv = n / EPV;
-    for (long long v = t0; v < nv; v += stride) {
+    // U vectors per thread per step: all U loads are issued before any of
+    // them is used, so each thread keeps 64 bytes of reads in flight through
+    // the activation arithmetic (one 16-byte vector at a time left HBM at
+    // 56 % of its bandwidth).
+    long long v = t0;
+    for (; v + (U - 1) * stride < nv; v += U * stride) {
+      uint4 b[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) b[u] = __ldcs(reinterpret_cast<const uint4*>(x) + v + u * stride);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        T* e = reinterpret_cast<T*>(&b[u]);
+        if (act == kActGeluErf) {
+#pragma unroll
+          for (int q = 0; q < EPV; ++q) e[q] = E<T>::t(gelu_value<T>(E<T>::f(e[q]), kActGeluErf));
+        } else {
+#pragma unroll
+          for (int q = 0; q < EPV; ++q) e[q] = E<T>::t(gelu_value<T>(E<T>::f(e[q]), act));
+        }
+        __stcs(reinterpret_cast<uint4*>(y) + v + u * stride, b[u]);
+      }
+    }
+    for (; v < nv; v += stride) {
       uint4 b = __ldcs(reinterpret_cast<const uint4*>(x) + v);
       T* e = reinterpret_cast<T*>(&b);
 #pragma unroll
-      for (int q = 0; q < EPV; ++q) e[q] = E<T>::t(apply_act(E<T>::f(e[q]), act));
+      for (int q = 0; q < EPV; ++q) e[q] = E<T>::t(gelu_value<T>(E<T>::f(e[q]), act));
       __stcs(reinterpret_cast<uint4*>(y) + v, b);
     }
-    for (long long i = nv * EPV + t0; i < n; i += stride) y[i] = E<T>::t(apply_act(E<T>::f(x[i]), act));
+    for (long long i = nv * EPV + t0; i < n; i += stride) y[i] = E<T>::t(gelu_value<T>(E<T>::f(x[i]), act));
   } else {
-    for (long long i = t0; i < n; i += stride) y[i] = E<T>::t(apply_act(E<T>::f(x[i]), act));
+    for (long long i = t0; i < n; i += stride) y[i] = E<T>::t(gelu_value<T>(E<T>::f(x[i]), act));
   }
 }
 

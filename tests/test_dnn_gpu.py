@@ -202,6 +202,31 @@ def test_softmax_strided_and_refusals(dnn):
     assert dnn.softmax(z, z) == N.NOT_SUPPORTED
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_gelu_erf_16bit_whole_range(dnn, dtype):
+    """16-bit erf-form GELU uses the Abramowitz & Stegun 7.1.26 erf (abs. error
+    <= 1.5e-7). Every value on a dense grid over [-12, 12] plus the type's
+    extremes is checked against the fp64 oracle: the far negative tail stays a
+    small negative number (no cancellation to 0 or NaN) and large positive x
+    returns x."""
+    grid = torch.linspace(-12, 12, 1 << 16, device="cuda")
+    big = torch.tensor([-60000.0, -1000.0, -40.0, 40.0, 1000.0, 60000.0], device="cuda")
+    x = torch.cat([grid, big]).to(dtype)
+    y = torch.empty_like(x)
+    assert dnn.gelu(x, y, 0) == N.SUCCESS
+    torch.cuda.synchronize()
+    got = y.float().cpu().numpy()
+    ref = oracle.gelu(x.float().cpu().numpy(), 0)
+    assert np.all(np.isfinite(got))
+    ok, nbad = close(got, ref, TOL_ABS, TOL_REL)
+    assert ok, nbad
+    xs = x.float().cpu().numpy()
+    tail = (xs < -3) & (xs > -8) & (np.abs(ref) > torch.finfo(dtype).tiny)  # representable as a normal value
+    # the tail keeps its sign and magnitude (A&S's relative error grows toward x = -8, where the
+    # values are below 1e-14; measured within 4 % there)
+    assert np.all(got[tail] < 0) and np.all(np.abs(got[tail] - ref[tail]) <= 6e-2 * np.abs(ref[tail]))
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("n", [1 << 20, 12345])
