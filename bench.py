@@ -553,6 +553,16 @@ def run_secondary(args, peaks, dev, stream):
     ms = _time(lambda: dh.gelu(x, y, 0), 20, stream)
     out["gelu"] = {"value": (nbytes - 8192 * 4) / ms / 1e6, "unit": "GB/s", "ms": ms,
                    "frac": (nbytes - 8192 * 4) / ms / 1e6 / hbm, "config": "bf16, 2^29 elements, erf form"}
+    # their backward passes: two tensors read, one written
+    dy0 = torch.randn(65536, 8192, device=dev, generator=g).to(torch.bfloat16)
+    nb3 = 3 * x.numel() * 2
+    ms = _time(lambda: dh.softmax_backward(y, dy0, y), 20, stream)
+    out["softmax_backward"] = {"value": nb3 / ms / 1e6, "unit": "GB/s", "ms": ms, "frac": nb3 / ms / 1e6 / hbm,
+                               "config": "bf16 [65536, 8192], dx written over y"}
+    ms = _time(lambda: dh.gelu_backward(x, dy0, y, 0), 20, stream)
+    out["gelu_backward"] = {"value": nb3 / ms / 1e6, "unit": "GB/s", "ms": ms, "frac": nb3 / ms / 1e6 / hbm,
+                            "config": "bf16, 2^29 elements, erf form"}
+    del dy0
     # norm backward on the same shape: x and dy read, dx written (saved statistics)
     dy = torch.randn(65536, 8192, device=dev, generator=g).to(torch.bfloat16)
     mean = torch.empty(65536, device=dev)

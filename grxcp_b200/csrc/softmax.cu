@@ -160,7 +160,8 @@ cudaError_t softmax_dispatch(int rows, int cols, const void* x, long long ldx, v
 // a 16-bit output's rounding. In the far negative tail, where x Phi(x) is tiny,
 // the relative error grows: 0.16 % at x = -5, a few % from x = -8 on (values
 // below 1e-14 there). fp32 outputs keep erff.
-__device__ __forceinline__ float gelu_erf_as(float x) {
+// Phi(x) = (1 + erf(x / sqrt 2)) / 2 by the same formula.
+__device__ __forceinline__ float phi_as(float x) {
   const float z = x * 0.7071067811865476f;
   const float a = fabsf(z);
   float t;
@@ -173,9 +174,9 @@ __device__ __forceinline__ float gelu_erf_as(float x) {
   float e;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-a * a * 1.4426950408889634f));
   const float q = poly * e;
-  const float one_plus_erf = z < 0.f ? q : 2.f - q;
-  return 0.5f * x * one_plus_erf;
+  return 0.5f * (z < 0.f ? q : 2.f - q);
 }
+__device__ __forceinline__ float gelu_erf_as(float x) { return x * phi_as(x); }
 
 // The forward GELU of one element: the erf form through gelu_erf_as for
 // 16-bit types, the shared epilogue activation otherwise.
@@ -258,6 +259,54 @@ __global__ void __launch_bounds__(kThreads) softmax_bwd_kernel(int cols, const T
   for (int c = threadIdx.x; c < cols; c += kThreads) xr[c] = E<T>::t(E<T>::f(yr[c]) * (E<T>::f(dr[c]) - tot));
 }
 
+// The same with the row's y and dy held in registers (16-byte vectors): each
+// read once from HBM, dx written once.
+template <typename T, int NV>
+__global__ void __launch_bounds__(kThreads) softmax_bwd_vec_kernel(int cols, const T* y, long long ldy,
+                                                                   const T* dy, long long lddy, T* dx,
+                                                                   long long lddx) {
+  constexpr int EPV = 16 / sizeof(T);
+  __shared__ float red[64];
+  const uint4* yr = reinterpret_cast<const uint4*>(y + (long long)blockIdx.x * ldy);
+  const uint4* dr = reinterpret_cast<const uint4*>(dy + (long long)blockIdx.x * lddy);
+  uint4* xr = reinterpret_cast<uint4*>(dx + (long long)blockIdx.x * lddx);
+  const int nvec = cols / EPV;
+  uint4 by[NV], bd[NV];
+  float s = 0.f;
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int vi = threadIdx.x + v * kThreads;
+    if (vi < nvec) {
+      by[v] = __ldcs(yr + vi);
+      bd[v] = __ldcs(dr + vi);
+    }
+  }
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int vi = threadIdx.x + v * kThreads;
+    if (vi < nvec) {
+      const T* ey = reinterpret_cast<const T*>(&by[v]);
+      const T* ed = reinterpret_cast<const T*>(&bd[v]);
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) s = fmaf(E<T>::f(ed[q]), E<T>::f(ey[q]), s);
+    }
+  }
+  const float tot = block_reduce<false>(s, red);
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int vi = threadIdx.x + v * kThreads;
+    if (vi < nvec) {
+      const T* ey = reinterpret_cast<const T*>(&by[v]);
+      const T* ed = reinterpret_cast<const T*>(&bd[v]);
+      uint4 o;
+      T* eo = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) eo[q] = E<T>::t(E<T>::f(ey[q]) * (E<T>::f(ed[q]) - tot));
+      __stcs(xr + vi, o);
+    }
+  }
+}
+
 // GELU derivative (Hendrycks & Gimpel), times dy:
 //   erf form:  Phi(x) + x phi(x),  phi(x) = exp(-x^2 / 2) / sqrt(2 pi)
 //   tanh form: 0.5 (1 + t) + 0.5 x (1 - t^2) sqrt(2/pi) (1 + 3 * 0.044715 x^2),
@@ -273,29 +322,97 @@ __device__ __forceinline__ float gelu_grad(float x, int act) {
   return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * k0 * fmaf(3.f * k1, x * x, 1.f);
 }
 
+// 16-bit types, erf form: Phi through phi_as and the density through the
+// SFU's 2^x (relative error ~1e-6, far under the output's rounding).
+template <typename T>
+__device__ __forceinline__ float gelu_grad_t(float x, int act) {
+  if (sizeof(T) == 2 && act == kActGeluErf) {
+    float e;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(-0.5f * x * x * 1.4426950408889634f));
+    return fmaf(x, 0.3989422804014327f * e, phi_as(x));
+  }
+  return gelu_grad(x, act);
+}
+
+// Grid-stride over 16-byte vectors of x and dy (two of each loaded per step
+// before any is used) when all three pointers are 16-byte aligned; element
+// by element otherwise and for the tail.
 template <typename T>
 __global__ void gelu_bwd_kernel(long long n, const T* x, const T* dy, T* dx,
-                                int act) {
+                                int act, int vec) {
+  constexpr int EPV = 16 / sizeof(T);
   const long long stride = (long long)gridDim.x * blockDim.x;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += stride)
-    dx[i] = E<T>::t(E<T>::f(dy[i]) * gelu_grad(E<T>::f(x[i]), act));
+  const long long t0 = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  long long done = 0;
+  if (vec) {
+    const long long nv = n / EPV;
+    long long v = t0;
+    for (; v + stride < nv; v += 2 * stride) {
+      uint4 bx[2], bd[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        bx[u] = __ldcs(reinterpret_cast<const uint4*>(x) + v + u * stride);
+        bd[u] = __ldcs(reinterpret_cast<const uint4*>(dy) + v + u * stride);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const T* ex = reinterpret_cast<const T*>(&bx[u]);
+        T* ed = reinterpret_cast<T*>(&bd[u]);
+#pragma unroll
+        for (int q = 0; q < EPV; ++q) ed[q] = E<T>::t(E<T>::f(ed[q]) * gelu_grad_t<T>(E<T>::f(ex[q]), act));
+        __stcs(reinterpret_cast<uint4*>(dx) + v + u * stride, bd[u]);
+      }
+    }
+    for (; v < nv; v += stride) {
+      const uint4 bx = __ldcs(reinterpret_cast<const uint4*>(x) + v);
+      uint4 bd = __ldcs(reinterpret_cast<const uint4*>(dy) + v);
+      const T* ex = reinterpret_cast<const T*>(&bx);
+      T* ed = reinterpret_cast<T*>(&bd);
+#pragma unroll
+      for (int q = 0; q < EPV; ++q) ed[q] = E<T>::t(E<T>::f(ed[q]) * gelu_grad_t<T>(E<T>::f(ex[q]), act));
+      __stcs(reinterpret_cast<uint4*>(dx) + v, bd);
+    }
+    done = nv * EPV;
+  }
+  for (long long i = done + t0; i < n; i += stride)
+    dx[i] = E<T>::t(E<T>::f(dy[i]) * gelu_grad_t<T>(E<T>::f(x[i]), act));
 }
 
 template <typename T>
 cudaError_t bwd_launch(int kind, long long rows_or_n, int cols, const void* a, long long lda, const void* b,
                        long long ldb, void* c, long long ldc, int act, int num_sms, cudaStream_t s) {
   if (kind == 0) {
-    ProfLaunch prof("softmax_bwd_kernel", dim3((unsigned)rows_or_n), dim3(kThreads), 0, s);
-    softmax_bwd_kernel<T><<<(unsigned)rows_or_n, kThreads, 0, s>>>(cols, static_cast<const T*>(a), lda,
-                                                                  static_cast<const T*>(b), ldb, static_cast<T*>(c),
-                                                                  ldc);
+    constexpr int EPV = 16 / sizeof(T);
+    const bool aligned = reinterpret_cast<uintptr_t>(a) % 16 == 0 && reinterpret_cast<uintptr_t>(b) % 16 == 0 &&
+                         reinterpret_cast<uintptr_t>(c) % 16 == 0 && cols % EPV == 0 &&
+                         (lda * (long long)sizeof(T)) % 16 == 0 && (ldb * (long long)sizeof(T)) % 16 == 0 &&
+                         (ldc * (long long)sizeof(T)) % 16 == 0;
+    const int nv = (cols / EPV + kThreads - 1) / kThreads;
+    const T* at = static_cast<const T*>(a);
+    const T* bt = static_cast<const T*>(b);
+    T* ct = static_cast<T*>(c);
+    const unsigned g = (unsigned)rows_or_n;
+    if (aligned && nv <= 4) {
+      ProfLaunch prof("softmax_bwd_vec_kernel", dim3(g), dim3(kThreads), 0, s);
+      switch (nv <= 1 ? 1 : nv <= 2 ? 2 : 4) {
+        case 1: softmax_bwd_vec_kernel<T, 1><<<g, kThreads, 0, s>>>(cols, at, lda, bt, ldb, ct, ldc); break;
+        case 2: softmax_bwd_vec_kernel<T, 2><<<g, kThreads, 0, s>>>(cols, at, lda, bt, ldb, ct, ldc); break;
+        default: softmax_bwd_vec_kernel<T, 4><<<g, kThreads, 0, s>>>(cols, at, lda, bt, ldb, ct, ldc); break;
+      }
+    } else {
+      ProfLaunch prof("softmax_bwd_kernel", dim3(g), dim3(kThreads), 0, s);
+      softmax_bwd_kernel<T><<<g, kThreads, 0, s>>>(cols, at, lda, bt, ldb, ct, ldc);
+    }
   } else {
-    long long blocks = (rows_or_n + kThreads - 1) / kThreads;
-    if (blocks > (long long)num_sms * 16) blocks = (long long)num_sms * 16;
+    const bool vec = reinterpret_cast<uintptr_t>(a) % 16 == 0 && reinterpret_cast<uintptr_t>(b) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(c) % 16 == 0;
+    long long blocks = (rows_or_n / (vec ? 16 / (long long)sizeof(T) : 1) + kThreads - 1) / kThreads;
+    if (blocks > (long long)num_sms * 8) blocks = (long long)num_sms * 8;
     if (blocks < 1) blocks = 1;
     ProfLaunch prof("gelu_bwd_kernel", dim3((unsigned)blocks), dim3(kThreads), 0, s);
     gelu_bwd_kernel<T><<<(unsigned)blocks, kThreads, 0, s>>>(rows_or_n, static_cast<const T*>(a),
-                                                            static_cast<const T*>(b), static_cast<T*>(c), act);
+                                                            static_cast<const T*>(b), static_cast<T*>(c), act,
+                                                            vec ? 1 : 0);
   }
   return cudaGetLastError();
 }

@@ -249,7 +249,7 @@ def test_gelu(dnn, dtype, mode, n):
 # ------------------------------------------------------------------ softmax / GELU backward
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("rows,cols", [(64, 4096), (33, 1000)])
+@pytest.mark.parametrize("rows,cols", [(64, 4096), (33, 1000), (16, 8192), (5, 1003)])
 def test_softmax_backward(dnn, dtype, rows, cols):
     """dx = y (dy - sum dy y) against the fp64 oracle, from the library's own forward output."""
     g = torch.Generator(device="cuda").manual_seed(rows + cols)
