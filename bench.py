@@ -634,6 +634,14 @@ def run_secondary(args, peaks, dev, stream):
     del a8, b8, i8a, i8b, c5
     torch.cuda.empty_cache()
 
+    # NHWC pooling (3x3, stride 2, pad 1, max) over a ResNet-style bf16 activation
+    xp = torch.randn(128, 56, 56, 256, device=dev, generator=g).to(torch.bfloat16)
+    yp = torch.empty(128, 28, 28, 256, device=dev, dtype=torch.bfloat16)
+    npb = (xp.numel() + yp.numel()) * 2
+    ms = _time(lambda: dh.pool2d(xp, yp, (3, 3), (1, 1), (2, 2), 0), 20, stream)
+    out["pool2d"] = {"value": npb / ms / 1e6, "unit": "GB/s", "ms": ms, "frac": npb / ms / 1e6 / hbm,
+                     "config": "bf16 NHWC [128, 56, 56, 256], 3x3 max, stride 2, pad 1; input read once + output"}
+    del xp, yp
     # config 1: fp32 SGEMM 512^3 and int8 512^3
     a = torch.rand(512 * 512, device=dev, generator=g) * 2 - 1
     b = torch.rand(512 * 512, device=dev, generator=g) * 2 - 1

@@ -135,7 +135,96 @@ cudaError_t launch_conv2d_direct(const ConvArgs& a, int num_sms, cudaStream_t s)
   return cudaGetLastError();
 }
 
+// 16-bit pooling with the channel count a multiple of 8 and 16-byte aligned
+// tensors: one thread per (output pixel, 8 consecutive channels), every
+// window tap one 16-byte load (a warp covers 512 contiguous bytes of a row of
+// the window). Same arithmetic per channel as pool2d_kernel.
+template <typename T>
+__global__ void pool2d_vec_kernel(PoolArgs a, const T* __restrict__ x, T* __restrict__ y) {
+  const int cv = a.c / 8;
+  const long long total = (long long)a.n * a.p * a.q * cv;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int c8 = (int)(e % cv);
+    long long t = e / cv;
+    const int q = (int)(t % a.q);
+    t /= a.q;
+    const int p = (int)(t % a.p);
+    const int n = (int)(t / a.p);
+    float m[8], sum[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      m[i] = -INFINITY;
+      sum[i] = 0.f;
+    }
+    int cnt = 0;
+    auto tap = [&](const uint4& b) {
+      const T* ev = reinterpret_cast<const T*>(&b);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float v = Cv<T>::f(ev[i]);
+        m[i] = fmaxf(m[i], v);
+        sum[i] += v;
+      }
+      ++cnt;
+    };
+    if (a.r * a.s <= 9) {
+      // Windows of up to 9 taps: every tap's load is issued before the first
+      // is used, so the taps' latencies overlap; taps are visited in the
+      // same row-major order as below.
+      uint4 b[9];
+      bool ok[9];
+#pragma unroll
+      for (int i = 0; i < 9; ++i) {
+        const int r = i / a.s, s2 = i - (i / a.s) * a.s;
+        const int hh = p * a.stride_h - a.pad_h + r, ww = q * a.stride_w - a.pad_w + s2;
+        ok[i] = i < a.r * a.s && hh >= 0 && hh < a.h && ww >= 0 && ww < a.w;
+        if (ok[i])
+          b[i] = __ldg(reinterpret_cast<const uint4*>(x + (((long long)n * a.h + hh) * a.w + ww) * a.c) + c8);
+      }
+#pragma unroll
+      for (int i = 0; i < 9; ++i)
+        if (ok[i]) tap(b[i]);
+    } else {
+      for (int r = 0; r < a.r; ++r) {
+        const int hh = p * a.stride_h - a.pad_h + r;
+        if (hh < 0 || hh >= a.h) continue;
+        for (int s2 = 0; s2 < a.s; ++s2) {
+          const int ww = q * a.stride_w - a.pad_w + s2;
+          if (ww < 0 || ww >= a.w) continue;
+          tap(__ldg(reinterpret_cast<const uint4*>(x + (((long long)n * a.h + hh) * a.w + ww) * a.c) + c8));
+        }
+      }
+    }
+    uint4 o;
+    T* eo = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float out;
+      if (a.mode == 0) out = cnt ? m[i] : 0.f;  // a window entirely in the padding yields 0
+      else if (a.mode == 1) out = sum[i] / (float)(a.r * a.s);
+      else out = cnt ? sum[i] / (float)cnt : 0.f;
+      eo[i] = Cv<T>::t(out);
+    }
+    reinterpret_cast<uint4*>(y)[e] = o;
+  }
+}
+
 cudaError_t launch_pool2d(const PoolArgs& a, int num_sms, cudaStream_t s) {
+  const bool vec = a.dtype != 0 && a.c % 8 == 0 && reinterpret_cast<uintptr_t>(a.x) % 16 == 0 &&
+                   reinterpret_cast<uintptr_t>(a.y) % 16 == 0;
+  if (vec) {
+    const unsigned g = grid_for((long long)a.n * a.p * a.q * (a.c / 8), num_sms);
+    ProfLaunch prof("pool2d_vec_kernel", dim3(g), dim3(256), 0, s);
+    if (a.dtype == 1)
+      pool2d_vec_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(a, static_cast<const __nv_bfloat16*>(a.x),
+                                                          static_cast<__nv_bfloat16*>(a.y));
+    else if (a.dtype == 2)
+      pool2d_vec_kernel<__half><<<g, 256, 0, s>>>(a, static_cast<const __half*>(a.x), static_cast<__half*>(a.y));
+    else
+      return cudaErrorNotSupported;
+    return cudaGetLastError();
+  }
   const long long total = (long long)a.n * a.p * a.q * a.c;
   const unsigned g = grid_for(total, num_sms);
   ProfLaunch prof("pool2d_kernel", dim3(g), dim3(256), 0, s);

@@ -108,10 +108,11 @@ def test_conv2d_errors(dh):
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("mode", [0, 1, 2])
 @pytest.mark.parametrize("window,pad,stride", [((3, 3), (1, 1), (2, 2)), ((2, 2), (0, 0), (2, 2)),
-                                               ((3, 2), (1, 0), (1, 2))])
-def test_pool2d(dh, dt, mode, window, pad, stride):
+                                               ((3, 2), (1, 0), (1, 2)), ((4, 3), (1, 1), (2, 2))])
+@pytest.mark.parametrize("c", [40, 36])  # 16-bit: 8-channel vector kernel / element kernel
+def test_pool2d(dh, dt, mode, window, pad, stride, c):
     g = torch.Generator().manual_seed(11)
-    x = torch.randn(2, 15, 17, 40, generator=g).to(dt)
+    x = torch.randn(2, 15, 17, c, generator=g).to(dt)
     ref = oracle.pool2d(x.double().numpy(), window, pad, stride, mode)
     y = torch.full(ref.shape, float("nan"), dtype=dt, device="cuda")
     assert dh.pool2d(x.cuda(), y, window, pad, stride, mode) == N.SUCCESS
